@@ -1,0 +1,109 @@
+/*
+ * int8conv_rules.h - shape algebra and per-family capability predicates.
+ *
+ * Header-only and dependency-free so the same rules are evaluated by the C ABI
+ * (runtime), the C++ drop-in header (compile time, constexpr) and the tests.
+ *
+ * Shape formulas follow include/conv_shape.cuh:22-35 of the reference exactly,
+ * including C++ integer division (truncation toward zero) in out_h/out_w.
+ */
+#ifndef INT8CONV_RULES_H_
+#define INT8CONV_RULES_H_
+
+#include <stdint.h>
+
+#include "int8conv.h"
+
+#ifdef __cplusplus
+#define I8C_RULE constexpr inline
+#else
+#define I8C_RULE static inline
+#endif
+
+/* TMA / kernel-geometry limits shared by every family.  They bound the
+ * im2col bounding-box corners ([-128,127] for a 4-D tensor map), the im2col
+ * tap offsets and the traversal strides (1..8) of the activation tensor map. */
+#define I8C_MAX_PAD 127
+#define I8C_MAX_TAP_SPAN 127
+#define I8C_MAX_STRIDE 8
+#define I8C_MAX_DIM (1 << 24)
+
+/* conv_shape.cuh:22-23 */
+I8C_RULE int32_t i8c_out_h(const int8conv_shape *s) {
+  return (s->h + 2 * s->pad_h - s->dilation_h * (s->r - 1) - 1) / s->stride_h + 1;
+}
+/* conv_shape.cuh:24-25 */
+I8C_RULE int32_t i8c_out_w(const int8conv_shape *s) {
+  return (s->w + 2 * s->pad_w - s->dilation_w * (s->s - 1) - 1) / s->stride_w + 1;
+}
+
+/* conv_shape.cuh:34-35 plus range checks the template got for free. */
+I8C_RULE int i8c_shape_valid(const int8conv_shape *s) {
+  return s != 0 && s->n > 0 && s->h > 0 && s->w > 0 && s->c > 0 && s->k > 0 &&
+         s->r > 0 && s->s > 0 && s->pad_h >= 0 && s->pad_w >= 0 &&
+         s->stride_h > 0 && s->stride_w > 0 && s->dilation_h > 0 &&
+         s->dilation_w > 0 && s->n <= I8C_MAX_DIM && s->h <= I8C_MAX_DIM &&
+         s->w <= I8C_MAX_DIM && s->c <= I8C_MAX_DIM && s->k <= I8C_MAX_DIM &&
+         s->r <= 4096 && s->s <= 4096 && s->pad_h <= I8C_MAX_DIM &&
+         s->pad_w <= I8C_MAX_DIM && s->stride_h <= I8C_MAX_DIM &&
+         s->stride_w <= I8C_MAX_DIM && s->dilation_h <= 4096 &&
+         s->dilation_w <= 4096 &&
+         /* conv_shape.cuh:34 */ s->c % 16 == 0 &&
+         /* conv_shape.cuh:35 */ i8c_out_h(s) > 0 && i8c_out_w(s) > 0 &&
+         /* NHWK index and NHWC extent stay inside int64 and the kernels' int32 row index */
+         (int64_t)s->n * i8c_out_h(s) * i8c_out_w(s) < ((int64_t)1 << 31) &&
+         (int64_t)s->n * s->h * s->w < ((int64_t)1 << 31);
+}
+
+/* Upper corner of the im2col bounding box along one spatial dimension such
+ * that the box holds exactly `count` traversal positions starting at -pad. */
+I8C_RULE int32_t i8c_upper_corner(int32_t extent, int32_t pad, int32_t stride,
+                                  int32_t count) {
+  return -pad + (count - 1) * stride + 1 - extent;
+}
+
+I8C_RULE int i8c_corner_ok(int32_t v) { return v >= -128 && v <= 127; }
+
+/* GENERIC: every valid shape whose activation tensor map can be encoded.
+ * Replaces the reference's generic family (generic_implicit_gemm.cuh), which
+ * accepted every shape with c % 16 == 0. */
+I8C_RULE int i8c_generic_eligible(const int8conv_shape *s) {
+  return i8c_shape_valid(s) && s->pad_h <= I8C_MAX_PAD && s->pad_w <= I8C_MAX_PAD &&
+         s->stride_h <= I8C_MAX_STRIDE && s->stride_w <= I8C_MAX_STRIDE &&
+         (int64_t)(s->r - 1) * s->dilation_h <= I8C_MAX_TAP_SPAN &&
+         (int64_t)(s->s - 1) * s->dilation_w <= I8C_MAX_TAP_SPAN &&
+         i8c_corner_ok(i8c_upper_corner(s->w, s->pad_w, s->stride_w, i8c_out_w(s))) &&
+         i8c_corner_ok(i8c_upper_corner(s->h, s->pad_h, s->stride_h, i8c_out_h(s)));
+}
+
+/* STRIP: one TMA-loaded row strip of (128 + S - 1) padded-row pixels is
+ * reused across the S filter columns.  Needs unit horizontal stride and
+ * dilation (the reference's own conditions, spatial_strip.cuh:11-15) and
+ * 2 <= S <= 16.  Every shape the reference's predicate accepts is accepted
+ * here; out_w % 128 and the r == 3 restriction are dropped because the B200
+ * kernel tiles the padded row instead of whole 128-pixel output rows. */
+I8C_RULE int i8c_strip_eligible(const int8conv_shape *s) {
+  return i8c_generic_eligible(s) && s->stride_w == 1 && s->dilation_w == 1 &&
+         s->s >= 2 && s->s <= 16 &&
+         i8c_corner_ok(i8c_upper_corner(s->w, s->pad_w, 1, i8c_out_w(s) + s->s - 1));
+}
+
+/* HALO and SPLITK predicates are defined by their kernels (int8conv_eligible);
+ * the constexpr forms below are the same rules. */
+I8C_RULE int i8c_halo_eligible(const int8conv_shape *s) {
+  return 0 * (s != 0);
+}
+I8C_RULE int i8c_splitk_eligible(const int8conv_shape *s) {
+  return 0 * (s != 0);
+}
+
+I8C_RULE int i8c_eligible(const int8conv_shape *s, int strategy) {
+  return strategy == INT8CONV_GENERIC   ? i8c_generic_eligible(s)
+         : strategy == INT8CONV_STRIP   ? i8c_strip_eligible(s)
+         : strategy == INT8CONV_HALO    ? i8c_halo_eligible(s)
+         : strategy == INT8CONV_SPLITK  ? i8c_splitk_eligible(s)
+                                        : 0;
+}
+
+#undef I8C_RULE
+#endif /* INT8CONV_RULES_H_ */

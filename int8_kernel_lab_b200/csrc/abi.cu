@@ -1,0 +1,187 @@
+// abi.cu - the extern "C" boundary declared in include/int8conv.h.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+#include "int8conv.h"
+#include "int8conv_rules.h"
+#include "launch.h"
+
+namespace i8c {
+extern std::atomic<uint64_t> g_wait_limit_ns;
+extern std::atomic<uint32_t> g_starve;
+extern std::atomic<uint64_t> g_launches;
+}  // namespace i8c
+
+namespace {
+
+bool aligned16(const void *p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// The kernel families implemented in this build.  A family whose kernel is
+// not built reports every shape as ineligible.
+bool family_built(int strategy) {
+  return strategy == INT8CONV_GENERIC;
+}
+
+int8conv_status launch_family(int strategy, const int8conv_shape *shape, const int8_t *input,
+                              const int8_t *filter, const int32_t *bias, int32_t *output,
+                              void *workspace, size_t workspace_bytes, void *stream) {
+  if (!i8c_shape_valid(shape)) return INT8CONV_BAD_SHAPE;
+  if (strategy == INT8CONV_AUTO) strategy = int8conv_select(shape);
+  if (strategy < 0 || strategy >= INT8CONV_NUM_STRATEGIES) return INT8CONV_BAD_ARGUMENT;
+  if (!int8conv_eligible(shape, strategy)) return INT8CONV_NOT_ELIGIBLE;
+  if (!aligned16(input) || !aligned16(filter) || !aligned16(bias) || !aligned16(output))
+    return INT8CONV_BAD_POINTER;
+  if (workspace_bytes < int8conv_workspace_bytes(shape, strategy))
+    return INT8CONV_WORKSPACE_TOO_SMALL;
+  (void)workspace;
+  const int8conv_status dev = i8c::check_device();
+  if (dev != INT8CONV_OK) return dev;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (strategy) {
+    case INT8CONV_GENERIC:
+      return i8c::launch_generic_impl(*shape, input, filter, bias, output, st);
+    default:
+      return INT8CONV_NOT_ELIGIBLE;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int int8conv_abi_version(void) { return INT8CONV_ABI_VERSION; }
+
+int int8conv_shape_valid(const int8conv_shape *shape) { return i8c_shape_valid(shape); }
+
+int8conv_status int8conv_shape_dims(const int8conv_shape *s, int8conv_dims *d) {
+  if (!i8c_shape_valid(s) || d == nullptr) return INT8CONV_BAD_SHAPE;
+  d->out_h = i8c_out_h(s);
+  d->out_w = i8c_out_w(s);
+  d->gemm_m = static_cast<int64_t>(s->n) * d->out_h * d->out_w;
+  d->gemm_n = s->k;
+  d->gemm_k = static_cast<int64_t>(s->r) * s->s * s->c;
+  d->input_elements = static_cast<int64_t>(s->n) * s->h * s->w * s->c;
+  d->filter_elements = static_cast<int64_t>(s->k) * s->r * s->s * s->c;
+  d->output_elements = d->gemm_m * d->gemm_n;
+  return INT8CONV_OK;
+}
+
+int int8conv_eligible(const int8conv_shape *shape, int strategy) {
+  if (!family_built(strategy)) return 0;
+  return i8c_eligible(shape, strategy);
+}
+
+int int8conv_select(const int8conv_shape *shape) {
+  // B200 dispatch policy (measured): strip where eligible, else generic.
+  if (int8conv_eligible(shape, INT8CONV_STRIP)) return INT8CONV_STRIP;
+  return INT8CONV_GENERIC;
+}
+
+size_t int8conv_workspace_bytes(const int8conv_shape *shape, int strategy) {
+  (void)shape;
+  (void)strategy;
+  return 0;
+}
+
+const char *int8conv_strategy_name(int strategy) {
+  switch (strategy) {
+    case INT8CONV_GENERIC:
+      return "generic";
+    case INT8CONV_STRIP:
+      return "strip";
+    case INT8CONV_HALO:
+      return "halo";
+    case INT8CONV_SPLITK:
+      return "splitk";
+    case INT8CONV_AUTO:
+      return "auto";
+    default:
+      return "unknown";
+  }
+}
+
+const char *int8conv_status_string(int status) {
+  switch (status) {
+    case INT8CONV_OK:
+      return "ok";
+    case INT8CONV_NOT_ELIGIBLE:
+      return "shape not eligible for this strategy";
+    case INT8CONV_BAD_SHAPE:
+      return "invalid convolution shape";
+    case INT8CONV_BAD_POINTER:
+      return "null or misaligned (16-byte) buffer";
+    case INT8CONV_CUDA_ERROR:
+      return "CUDA error";
+    case INT8CONV_DEVICE_TIMEOUT:
+      return "device wait timed out";
+    case INT8CONV_WORKSPACE_TOO_SMALL:
+      return "workspace too small";
+    case INT8CONV_UNSUPPORTED_DEVICE:
+      return "device is not sm_100";
+    case INT8CONV_BAD_ARGUMENT:
+      return "bad argument";
+    default:
+      return "unknown status";
+  }
+}
+
+int8conv_status int8conv_launch(int strategy, const int8conv_shape *shape, const int8_t *input,
+                                const int8_t *filter, const int32_t *bias, int32_t *output,
+                                void *workspace, size_t workspace_bytes, void *stream) {
+  return launch_family(strategy, shape, input, filter, bias, output, workspace,
+                       workspace_bytes, stream);
+}
+
+int8conv_status int8conv_launch_generic(const int8conv_shape *shape, const int8_t *input,
+                                        const int8_t *filter, const int32_t *bias,
+                                        int32_t *output, void *stream) {
+  return launch_family(INT8CONV_GENERIC, shape, input, filter, bias, output, nullptr, 0, stream);
+}
+
+int8conv_status int8conv_launch_spatial_strip(const int8conv_shape *shape, const int8_t *input,
+                                              const int8_t *filter, const int32_t *bias,
+                                              int32_t *output, void *stream) {
+  return launch_family(INT8CONV_STRIP, shape, input, filter, bias, output, nullptr, 0, stream);
+}
+
+int8conv_status int8conv_launch_halo(const int8conv_shape *shape, const int8_t *input,
+                                     const int8_t *filter, const int32_t *bias, int32_t *output,
+                                     void *stream) {
+  return launch_family(INT8CONV_HALO, shape, input, filter, bias, output, nullptr, 0, stream);
+}
+
+int8conv_status int8conv_launch_splitk(const int8conv_shape *shape, const int8_t *input,
+                                       const int8_t *filter, const int32_t *bias,
+                                       int32_t *output, void *workspace, size_t workspace_bytes,
+                                       void *stream) {
+  return launch_family(INT8CONV_SPLITK, shape, input, filter, bias, output, workspace,
+                       workspace_bytes, stream);
+}
+
+int8conv_status int8conv_device_status(void) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return INT8CONV_CUDA_ERROR;
+  i8c::DeviceInfo &d = i8c::device_info();
+  if (d.status == nullptr) return INT8CONV_CUDA_ERROR;
+  uint32_t word = 0;
+  if (cudaMemcpy(&word, d.status, sizeof(word), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return INT8CONV_CUDA_ERROR;
+  if (word != 0) {
+    const uint32_t zero = 0;
+    if (cudaMemcpy(d.status, &zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess)
+      return INT8CONV_CUDA_ERROR;
+    return INT8CONV_DEVICE_TIMEOUT;
+  }
+  return INT8CONV_OK;
+}
+
+void int8conv_set_wait_limit_ns(uint64_t ns) {
+  i8c::g_wait_limit_ns.store(ns == 0 ? 2000000000ull : ns);
+}
+
+void int8conv_debug_starve_producer(int on) { i8c::g_starve.store(on ? 1u : 0u); }
+
+uint64_t int8conv_launch_count(void) { return i8c::g_launches.load(); }
+
+}  // extern "C"

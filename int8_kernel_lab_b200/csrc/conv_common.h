@@ -1,0 +1,44 @@
+// conv_common.h - host/device types shared by the kernel families.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "int8conv.h"
+
+namespace i8c {
+
+// Geometry of one launch, in GEMM terms (M = output pixels, N = output
+// channels, reduction = R*S taps x channel blocks).  Derived on the host from
+// int8conv_shape with the formulas of the reference's conv_shape.cuh:22-28.
+struct ConvGeom {
+  int32_t M;         // n * out_h * out_w
+  int32_t K;         // output channels (GEMM N)
+  int32_t P, Q;      // out_h, out_w
+  int32_t PQ;        // out_h * out_w
+  int32_t R, S;
+  int32_t pad_h, pad_w;
+  int32_t stride_h, stride_w;
+  int32_t dil_h, dil_w;
+  int32_t cblocks;   // channel blocks per tap
+  int32_t kblocks;   // R * S * cblocks
+  int32_t bn;        // CTA tile width in output channels (multiple of 16, <= 256)
+  int32_t acc_stride;// TMEM columns between the two accumulator buffers
+  int32_t tmem_cols; // TMEM columns allocated (power of two)
+  int32_t stages;    // shared-memory ring depth
+  int32_t m_tiles, n_tiles, num_tiles;
+};
+
+// Failure-detection controls passed to every kernel.
+struct RunCtl {
+  uint32_t *status;     // device status word (bit set on a wait timeout)
+  uint64_t wait_ns;     // per-wait limit
+  uint32_t starve;      // test hook: producer issues no copies
+};
+
+constexpr int kBlockM = 128;         // MMA M (rows = output pixels)
+constexpr int kThreads = 192;        // 6 warps
+constexpr int kMaxSmem = 232448;     // 227 KB opt-in limit per block on sm_100
+
+}  // namespace i8c

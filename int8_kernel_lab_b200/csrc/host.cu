@@ -1,0 +1,212 @@
+// host.cu - per-device state, tensor-map encoding and run controls.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "launch.h"
+
+namespace i8c {
+
+// Module-scope status word: kernels OR timeout bits into it, the host reads
+// and clears it in int8conv_device_status().  One copy per device.
+__device__ uint32_t g_device_status;
+
+std::atomic<uint64_t> g_wait_limit_ns{2000000000ull};
+std::atomic<uint32_t> g_starve{0};
+std::atomic<uint64_t> g_launches{0};
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_device_mutex;
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+PFN_cuTensorMapEncodeIm2col_v12000 g_encode_im2col = nullptr;
+int g_driver_version = 0;
+std::once_flag g_driver_once;
+
+void load_driver_entry_points() {
+  cudaDriverEntryPointQueryResult q;
+  void *fn = nullptr;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+          cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  fn = nullptr;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q) ==
+          cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_encode_im2col = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(fn);
+  cudaDriverGetVersion(&g_driver_version);
+}
+
+// Small cache of encoded maps: a launch with the same buffers and shape reuses
+// the 128-byte descriptor instead of re-encoding it on every call.
+struct MapKey {
+  int32_t device, kind, channels, rows, count_w, pad;
+  int8conv_shape shape;
+  const void *ptr;
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool used;
+};
+constexpr int kMapCache = 128;
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+std::mutex g_map_mutex;
+
+bool map_lookup(const MapKey &key, CUtensorMap *map) {
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  for (int i = 0; i < kMapCache; ++i) {
+    if (g_maps[i].used && memcmp(&g_maps[i].key, &key, sizeof(MapKey)) == 0) {
+      *map = g_maps[i].map;
+      return true;
+    }
+  }
+  return false;
+}
+
+void map_store(const MapKey &key, const CUtensorMap &map) {
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  MapEntry &e = g_maps[g_map_next];
+  g_map_next = (g_map_next + 1) % kMapCache;
+  e.key = key;
+  e.map = map;
+  e.used = true;
+}
+
+MapKey make_key(int kind, const int8conv_shape &s, const void *ptr, int channels, int rows,
+                int count_w) {
+  MapKey k;
+  memset(&k, 0, sizeof(k));
+  k.device = device_info().device;
+  k.kind = kind;
+  k.channels = channels;
+  k.rows = rows;
+  k.count_w = count_w;
+  k.shape = s;
+  k.ptr = ptr;
+  return k;
+}
+
+CUtensorMapSwizzle swizzle_for(int bytes) {
+  switch (bytes) {
+    case 128:
+      return CU_TENSOR_MAP_SWIZZLE_128B;
+    case 64:
+      return CU_TENSOR_MAP_SWIZZLE_64B;
+    case 32:
+      return CU_TENSOR_MAP_SWIZZLE_32B;
+    default:
+      return CU_TENSOR_MAP_SWIZZLE_NONE;
+  }
+}
+
+}  // namespace
+
+DeviceInfo &device_info() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) dev = 0;
+  DeviceInfo &d = g_devices[dev];
+  if (d.device != dev) {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (d.device != dev) {
+      cudaDeviceProp prop;
+      if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess) {
+        d.sm_count = prop.multiProcessorCount;
+        d.cc_major = prop.major;
+        d.cc_minor = prop.minor;
+      }
+      void *addr = nullptr;
+      if (cudaGetSymbolAddress(&addr, g_device_status) == cudaSuccess)
+        d.status = static_cast<uint32_t *>(addr);
+      std::atomic_thread_fence(std::memory_order_release);
+      d.device = dev;
+    }
+  }
+  return d;
+}
+
+int8conv_status check_device() {
+  DeviceInfo &d = device_info();
+  if (d.sm_count == 0) return INT8CONV_CUDA_ERROR;
+  if (d.cc_major != 10) return INT8CONV_UNSUPPORTED_DEVICE;
+  return INT8CONV_OK;
+}
+
+RunCtl run_ctl() {
+  RunCtl c;
+  c.status = device_info().status;
+  c.wait_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+  c.starve = g_starve.load(std::memory_order_relaxed);
+  return c;
+}
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool ensure_smem_attr(const void *kernel, int bytes) {
+  // Idempotent and cheap; the runtime caches the attribute per function.
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+         cudaSuccess;
+}
+
+int8conv_status activation_map_im2col(const int8conv_shape &s, const int8_t *x, int channels,
+                                      int pixels, int count_w, CUtensorMap *map) {
+  const MapKey key = make_key(1, s, x, channels, pixels, count_w);
+  if (map_lookup(key, map)) return INT8CONV_OK;
+  std::call_once(g_driver_once, load_driver_entry_points);
+  if (!g_encode_im2col) return INT8CONV_CUDA_ERROR;
+  const int32_t out_h = (s.h + 2 * s.pad_h - s.dilation_h * (s.r - 1) - 1) / s.stride_h + 1;
+  cuuint64_t dims[4] = {(cuuint64_t)s.c, (cuuint64_t)s.w, (cuuint64_t)s.h, (cuuint64_t)s.n};
+  cuuint64_t strides[3] = {(cuuint64_t)s.c, (cuuint64_t)s.w * s.c, (cuuint64_t)s.h * s.w * s.c};
+  // Bounding box per image: traversal starts at -pad and holds exactly
+  // count_w x out_h positions (stride apart); the upper corner is chosen so.
+  int lower[2] = {-s.pad_w, -s.pad_h};
+  int upper[2] = {-s.pad_w + (count_w - 1) * s.stride_w + 1 - s.w,
+                  -s.pad_h + (out_h - 1) * s.stride_h + 1 - s.h};
+  cuuint32_t estr[4] = {1, (cuuint32_t)s.stride_w, (cuuint32_t)s.stride_h, 1};
+  CUresult rc = g_encode_im2col(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t *>(x),
+                                dims, strides, lower, upper, (cuuint32_t)channels,
+                                (cuuint32_t)pixels, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                swizzle_for(channels), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (rc != CUDA_SUCCESS) return INT8CONV_CUDA_ERROR;
+  // Driver <= 13.1 mis-handles im2col maps over tensors smaller than 128 KB
+  // unless bit 21 of the descriptor's second word is cleared (the same
+  // workaround CUTLASS applies in cute/atom/copy_traits_sm90_im2col.hpp).
+  const uint64_t bytes = (uint64_t)s.n * s.h * s.w * s.c;
+  if (g_driver_version <= 13010 && bytes < 131072)
+    reinterpret_cast<uint64_t *>(map)[1] &= ~(1ull << 21);
+  map_store(key, *map);
+  return INT8CONV_OK;
+}
+
+int8conv_status filter_map_tiled(const int8conv_shape &s, const int8_t *w, int channels,
+                                 int rows, CUtensorMap *map) {
+  const MapKey key = make_key(2, s, w, channels, rows, 0);
+  if (map_lookup(key, map)) return INT8CONV_OK;
+  std::call_once(g_driver_once, load_driver_entry_points);
+  if (!g_encode_tiled) return INT8CONV_CUDA_ERROR;
+  cuuint64_t dims[3] = {(cuuint64_t)s.c, (cuuint64_t)s.r * s.s, (cuuint64_t)s.k};
+  cuuint64_t strides[2] = {(cuuint64_t)s.c, (cuuint64_t)s.r * s.s * s.c};
+  cuuint32_t box[3] = {(cuuint32_t)channels, 1, (cuuint32_t)rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult rc = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(w),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               swizzle_for(channels), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (rc != CUDA_SUCCESS) return INT8CONV_CUDA_ERROR;
+  map_store(key, *map);
+  return INT8CONV_OK;
+}
+
+}  // namespace i8c

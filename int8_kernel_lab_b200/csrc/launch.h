@@ -1,0 +1,54 @@
+// launch.h - host-side services shared by the kernel families: per-device
+// properties, TMA tensor-map encoding (with a small cache), the device status
+// word and the failure-detection controls.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "conv_common.h"
+#include "int8conv.h"
+
+namespace i8c {
+
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  uint32_t *status = nullptr;   // address of the module's __device__ status word
+};
+
+// Properties of the calling thread's current device (cached per device).
+DeviceInfo &device_info();
+
+// INT8CONV_OK when the current device is an sm_100 part.
+int8conv_status check_device();
+
+// Run controls for the next launch: status word, wait limit, starve hook.
+RunCtl run_ctl();
+
+void note_launch();
+
+// Sets the dynamic shared-memory limit of `kernel` once per device.
+bool ensure_smem_attr(const void *kernel, int bytes);
+
+// im2col tensor map over the NHWC activations: `channels` bytes per pixel
+// (swizzle = channels bytes), `pixels` traversal positions per load, and a
+// bounding box holding `count_w` positions per row (out_w for GENERIC,
+// out_w + s - 1 for STRIP) and out_h rows.
+int8conv_status activation_map_im2col(const int8conv_shape &s, const int8_t *x, int channels,
+                                      int pixels, int count_w, CUtensorMap *map);
+
+// Tiled tensor map over the KRSC filter viewed as [K][R*S][C], box
+// (channels, 1, rows).
+int8conv_status filter_map_tiled(const int8conv_shape &s, const int8_t *w, int channels,
+                                 int rows, CUtensorMap *map);
+
+// Family launchers (valid, eligible shape; pointers already checked).
+int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                    const int32_t *b, int32_t *y, cudaStream_t stream);
+int8conv_status launch_strip_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                  const int32_t *b, int32_t *y, cudaStream_t stream);
+
+}  // namespace i8c
