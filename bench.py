@@ -1,0 +1,454 @@
+#!/usr/bin/env python3
+"""INT8 convolution throughput on B200: effective TOPS and roofline fraction.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: BASELINE config 5a, the batch-scaled stress conv (N=256, H=W=56,
+C=K=256, 3x3, stride 1, pad 1), int8 uniform on [-128,127], int32 bias on
+[-65536,65536], seeded.  With N GPUs (one process per GPU under torchrun) the
+batch is split evenly: rank r convolves images [r*256/N, (r+1)*256/N); no
+collective is on the data path (NCCL only gathers outputs for verification,
+outside the timed region).  A step is one convolution of the whole batch.
+
+Printed (rank 0, one JSON line):
+  value     whole-job effective TOPS = 2*N*P*Q*K*C*R*S*steps / max-over-ranks
+            device time (CUDA events on the launching stream, inputs resident)
+  e2e       same metric through the public API with pinned host buffers:
+            host->device copy of each step's input shard, filter and bias,
+            the launch, and the device->host copy of the NHWK output
+  roofline  the conv kernel's achieved TOPS vs the INT8 dense peak
+  cpu_baseline  the CPU oracle on the host cores (N=1 only), on whole images
+            of the same workload; the GPU outputs of those images are compared
+            with it (bit-exact) and the result is reported as `verified`
+--impl reference times the reference's own CPU implementation of the path
+(reference_value of src/conv_lab.cu:39-66, built from the reference sources
+into oracle/_ref) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import ctypes
+import datetime
+import io
+import json
+import math
+import os
+import shutil
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "INT8 conv TOPS & % of B200 INT8 tensor peak at 1/2/4/8 GPUs vs host-CPU oracle"
+DEFAULT_WORKLOAD = "cfg5a_stress_3x3"
+NOMINAL_INT8_TOPS = 4500.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--strategy", default="auto")
+    ap.add_argument("--e2e-steps", type=int, default=8)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def sustained_peak():
+    """2x the measured sustained bf16 figure (seconds-long loop under the power cap)."""
+    try:
+        data = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return 2.0 * float(data["bf16_tflops_sustained"])
+    except (OSError, KeyError, ValueError):
+        return 2.0 * 1400.0
+
+
+def measured_peaks():
+    """INT8 dense peak used as the roofline denominator.
+
+    MEASURED_PEAKS.json (driver-written) holds a measured cuBLAS bf16 dense
+    throughput; B200's dense INT8 rate is twice its bf16 rate (4.5 vs 2.25
+    PFLOP/s nominal), so the INT8 denominator is 2x the measured bf16 burst
+    figure.  Without the file the pool's fallback (1.59 PFLOP/s bf16) is used.
+    """
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return 2.0 * float(data["bf16_tflops"]), "2x measured bf16 cuBLAS burst (MEASURED_PEAKS.json)"
+    except (OSError, KeyError, ValueError):
+        return 2.0 * 1590.0, "2x fallback bf16 1.59 PFLOP/s"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.proc = None
+        self.out = None
+        if shutil.which("nvidia-smi"):
+            self.out = tempfile.TemporaryFile(mode="w+")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-i", gpu_id, "-lms", "100"], stdout=self.out, stderr=subprocess.DEVNULL)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.seek(0)
+        rows = [r for r in csv.reader(io.StringIO(self.out.read())) if len(r) >= 9]
+        if not rows:
+            return None
+        sm = sorted(float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def shard(n: int, rank: int, world: int):
+    """Images [start, stop) of `rank`: an even split of the batch."""
+    per = n // world
+    extra = n % world
+    start = rank * per + min(rank, extra)
+    return start, start + per + (1 if rank < extra else 0)
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0  # only rank 0 runs and prints the reference arm
+    import numpy as np
+
+    import int8_kernel_lab_b200 as m
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pyoracle  # noqa: E402  (test infrastructure: the reference leg only)
+
+    shape = m.load_workloads()[args.workload]
+    x, w, b = m.make_inputs(shape)
+    threads = os.cpu_count() or 1
+    binary = pyoracle.ref_binary(args.workload)
+    rows_per_image = shape.out_h * shape.out_w
+    # Size each step so warmup + steps fit in about two minutes.
+    budget_s = 120.0 / max(1, args.steps + args.warmup)
+    probe_rows = min(64, shape.gemm_m)
+    if binary is not None:
+        kind = "reference"
+        _, t = pyoracle.ref_cpu_rows(args.workload, x, w, b, 0, probe_rows, threads)
+    else:
+        kind = "port"
+        t0 = time.perf_counter()
+        pyoracle.conv_rows(shape, x, w, b, 0, probe_rows, threads)
+        t = time.perf_counter() - t0
+    rows = int(max(1, min(shape.gemm_m, probe_rows * budget_s / max(t, 1e-6))))
+    total_steps = args.steps + args.warmup
+    if kind == "reference":
+        with tempfile.TemporaryDirectory() as tmp:
+            paths = [os.path.join(tmp, n) for n in ("x.bin", "w.bin", "b.bin", "y.bin")]
+            x.tofile(paths[0]); w.tofile(paths[1]); b.tofile(paths[2])
+            proc = subprocess.run([str(binary), "cpu", *paths, "0", str(rows), str(threads),
+                                   str(total_steps)], check=True, capture_output=True, text=True)
+            res = json.loads(proc.stdout.strip().splitlines()[-1])
+            step_s = res["step_seconds"][args.warmup:]
+    else:
+        step_s = []
+        for i in range(total_steps):
+            t0 = time.perf_counter()
+            pyoracle.conv_rows(shape, x, w, b, 0, rows, threads)
+            if i >= args.warmup:
+                step_s.append(time.perf_counter() - t0)
+    sec = sum(step_s) / len(step_s)
+    ops = 2.0 * rows * shape.k * shape.gemm_k
+    value = ops / sec / 1e12
+    sample = (f"output rows [0, {rows}) of {args.workload} ({rows / rows_per_image:.3f} of one "
+              f"image, all {shape.k} channels) per step, {threads} threads")
+    line = {
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "TOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": workload_config(shape, args, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(shape, args, world):
+    return {
+        "workload": args.workload,
+        "shape": {f: getattr(shape, f) for f in ("n", "h", "w", "c", "k", "r", "s", "pad_h",
+                                                 "pad_w", "stride_h", "stride_w", "dilation_h",
+                                                 "dilation_w")},
+        "out_hw": [shape.out_h, shape.out_w],
+        "ops_per_step": shape.ops,
+        "parallelism": f"batch-sharded x{world} (no data-path collective)",
+        "values": "int8 uniform [-128,127], bias int32 uniform [-65536,65536], seed 20260925",
+    }
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    import int8_kernel_lab_b200 as m
+    from int8_kernel_lab_b200 import _abi
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    full = m.load_workloads()[args.workload]
+    lo, hi = shard(full.n, rank, world)
+    local_shape = full.with_batch(hi - lo)
+    x, w, b = m.make_inputs(full)
+    per_image_in = full.h * full.w * full.c
+    x_local = x[lo * per_image_in:hi * per_image_in]
+    strategy = local_shape.select() if args.strategy == "auto" else args.strategy
+    code = _abi.STRATEGIES[strategy]
+    cshape = local_shape.c_struct()
+
+    # Device buffers.  Enough input/output sets rotate that a step never finds
+    # its operands in L2 (working set >= 2x L2 across consecutive steps).
+    props = torch.cuda.get_device_properties(local)
+    l2 = int(getattr(props, "L2_cache_size", 126 * 2**20))
+    per_set = x_local.nbytes + 4 * local_shape.output_elements
+    sets = max(1, math.ceil(2 * l2 / per_set)) if per_set < 2 * l2 else 1
+    dw = torch.from_numpy(w).cuda()
+    db = torch.from_numpy(b).cuda()
+    dxs = [torch.from_numpy(x_local).cuda() for _ in range(sets)]
+    dys = [torch.empty(local_shape.output_elements, dtype=torch.int32, device="cuda")
+           for _ in range(sets)]
+    stream = torch.cuda.current_stream()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    launch = _abi.lib.int8conv_launch
+    args_per_set = [(code, cshape, dxs[i].data_ptr(), dw.data_ptr(), db.data_ptr(),
+                     dys[i].data_ptr(), None, 0, sptr) for i in range(sets)]
+
+    def step(i):
+        st = launch(*args_per_set[i % sets])
+        if st != _abi.OK:
+            raise _abi.Int8ConvError(st, "bench launch")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    gpu_uuid = "GPU-" + str(props.uuid) if hasattr(props, "uuid") else str(local)
+    sampler = ClockSampler(gpu_uuid) if rank == 0 else None
+    launches0 = m.launch_count()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    launches = m.launch_count() - launches0
+    clocks = sampler.stop() if sampler else None
+    elapsed_ms = start.elapsed_time(stop)
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    if m.device_status() != _abi.OK:
+        raise SystemExit("device status not OK after the timed region")
+    ms_per_step = max_ms / args.steps
+    value = full.ops / (ms_per_step * 1e-3) / 1e12
+    local_launch_ms = elapsed_ms / args.steps  # one kernel per step on this stream
+    achieved = local_shape.ops / (local_launch_ms * 1e-3) / 1e12
+    peak, peak_src = measured_peaks()
+
+    # ---- end to end through the public API, host buffers ----
+    hx = torch.from_numpy(x_local).pin_memory()
+    hw = torch.from_numpy(w).pin_memory()
+    hb = torch.from_numpy(b).pin_memory()
+    hy = torch.empty(local_shape.output_elements, dtype=torch.int32).pin_memory()
+    ex, ew, eb, ey = dxs[0], dw, db, dys[0]
+
+    def e2e_step():
+        ex.copy_(hx, non_blocking=True)
+        ew.copy_(hw, non_blocking=True)
+        eb.copy_(hb, non_blocking=True)
+        m.launch(strategy, local_shape, ex, ew, eb, ey)
+        hy.copy_(ey, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item()) / args.e2e_steps
+    h2d = int(hx.numel() + hw.numel() + 4 * hb.numel()) * world
+    d2h = int(4 * hy.numel()) * world
+
+    # ---- verification / CPU baseline ----
+    y_local = hy.numpy()  # output of the last e2e step (identical inputs)
+    cpu = None
+    verify = None
+    if world == 1 and not args.no_cpu_baseline and rank == 0:
+        cpu = cpu_baseline(full, x, w, b, y_local, args)
+    elif dist is not None:
+        verify = verify_sharded(full, dxs, dys, dw, db, local_shape, x, strategy, dist, rank,
+                                world, lo, hi)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": dict(workload_config(full, args, world), strategy=strategy,
+                           images_per_rank=hi - lo,
+                           l2=("inputs larger than L2: %d rotating input/output set(s), "
+                               "%.0f MB per set, L2 %.0f MB" % (sets, per_set / 1e6, l2 / 1e6))),
+            "e2e": {"value": full.ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TOPS", "frac": achieved / peak, "peak_source": peak_src,
+                         "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
+                         "frac_of_sustained": achieved / sustained_peak(),
+                         "kernel": f"conv_kernel ({strategy})",
+                         "launch_ms": local_launch_ms, "traffic": traffic_per_launch(args,
+                                                                                     local_shape)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        if verify is not None:
+            line["verified_sharded_vs_single_gpu"] = verify
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def traffic_per_launch(args, local_shape):
+    """DRAM bytes per launch from the committed ncu capture of this kernel
+    (profiles/traffic.json), scaled by images, or None if not captured."""
+    path = ROOT / "profiles" / "traffic.json"
+    try:
+        data = json.loads(path.read_text())[args.workload]
+        return data["bytes_per_image"] * local_shape.n
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def cpu_baseline(shape, x, w, b, y_gpu, args):
+    """Times the oracle port (oracle/conv_oracle.c) on whole images of the
+    workload with all host threads and checks the GPU output of those images."""
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pyoracle  # noqa: E402  (test infrastructure: the cpu_baseline leg only)
+
+    threads = os.cpu_count() or 1
+    rows = shape.out_h * shape.out_w
+    first = pyoracle.conv_rows(shape, x, w, b, 0, rows, threads)  # warm
+    t0 = time.perf_counter()
+    first = pyoracle.conv_rows(shape, x, w, b, 0, rows, threads)
+    t1 = time.perf_counter() - t0
+    images = int(max(1, min(shape.n - 1, args.cpu_seconds / max(t1, 1e-6) - 1)))
+    # images [n - images, n): the end of the batch, a different rank's shard at N>1
+    lo = shape.n - images
+    t0 = time.perf_counter()
+    tail = pyoracle.conv_rows(shape, x, w, b, lo * rows, shape.n * rows, threads)
+    sec = time.perf_counter() - t0
+    ops = 2.0 * images * rows * shape.k * shape.gemm_k
+    k = shape.k
+    ok = bool(np.array_equal(y_gpu[:rows * k], first) and
+              np.array_equal(y_gpu[lo * rows * k:], tail))
+    return {"value": ops / sec / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{images} whole image(s) of {args.workload} (images {lo}..{shape.n - 1}), "
+                      f"{ops / 1e9:.1f} Gop in {sec:.2f} s",
+            "verified": ok, "verified_images": f"0 and {lo}..{shape.n - 1}"}
+
+
+def verify_sharded(full, dxs, dys, dw, db, local_shape, x, strategy, dist, rank, world, lo, hi):
+    """NCCL gathers every rank's NHWK slice to rank 0, which recomputes the
+    whole batch on its own GPU and compares bit-exactly (outside timing)."""
+    import torch
+
+    import int8_kernel_lab_b200 as m
+    counts = [shard(full.n, r, world) for r in range(world)]
+    per_img = full.out_h * full.out_w * full.k
+    parts = [torch.empty((c1 - c0) * per_img, dtype=torch.int32, device="cuda")
+             for c0, c1 in counts]
+    mine = dys[0]
+    if rank == 0:
+        dist.gather(mine, gather_list=parts, dst=0)
+        gathered = torch.cat(parts)
+        xall = torch.from_numpy(x).cuda()
+        yall = torch.empty(full.output_elements, dtype=torch.int32, device="cuda")
+        m.launch(strategy if full.eligible(strategy) else "generic", full, xall, dw, db, yall)
+        torch.cuda.synchronize()
+        return bool(torch.equal(gathered, yall))
+    dist.gather(mine, dst=0)
+    return None
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

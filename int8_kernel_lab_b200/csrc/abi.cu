@@ -21,7 +21,7 @@ bool aligned16(const void *p) { return p != nullptr && (reinterpret_cast<uintptr
 // The kernel families implemented in this build.  A family whose kernel is
 // not built reports every shape as ineligible.
 bool family_built(int strategy) {
-  return strategy == INT8CONV_GENERIC;
+  return strategy == INT8CONV_GENERIC || strategy == INT8CONV_STRIP;
 }
 
 int8conv_status launch_family(int strategy, const int8conv_shape *shape, const int8_t *input,
@@ -42,6 +42,8 @@ int8conv_status launch_family(int strategy, const int8conv_shape *shape, const i
   switch (strategy) {
     case INT8CONV_GENERIC:
       return i8c::launch_generic_impl(*shape, input, filter, bias, output, st);
+    case INT8CONV_STRIP:
+      return i8c::launch_strip_impl(*shape, input, filter, bias, output, st);
     default:
       return INT8CONV_NOT_ELIGIBLE;
   }

@@ -26,8 +26,17 @@ struct ConvGeom {
   int32_t bn;        // CTA tile width in output channels (multiple of 16, <= 256)
   int32_t acc_stride;// TMEM columns between the two accumulator buffers
   int32_t tmem_cols; // TMEM columns allocated (power of two)
-  int32_t stages;    // shared-memory ring depth
+  int32_t stages;    // shared-memory ring depth (B ring; also A for GENERIC)
   int32_t m_tiles, n_tiles, num_tiles;
+  // STRIP only: the M dimension runs over padded-row positions
+  // (n, oy, j) with j in [0, Wp), Wp = out_w + S - 1; positions j >= out_w
+  // are computed and discarded.
+  int32_t Wp;        // padded row width
+  int32_t PWp;       // out_h * Wp
+  int32_t Mp;        // n * out_h * Wp
+  int32_t strip_px;  // pixels per strip load (128 + S - 1)
+  int32_t a_rows;    // rows reserved per strip stage (strip_px rounded up to 8)
+  int32_t a_stages;  // strip ring depth
 };
 
 // Failure-detection controls passed to every kernel.

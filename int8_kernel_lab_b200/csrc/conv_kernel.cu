@@ -1,0 +1,534 @@
+// conv_kernel.cu - GENERIC and STRIP families: INT8 implicit-GEMM convolution
+// on tcgen05 tensor cores.
+//
+// Contract of the reference kernels it replaces (generic_implicit_gemm_kernel,
+// include/generic_implicit_gemm.cuh:90-153 / :170-227, and spatial_strip_kernel,
+// include/spatial_strip.cuh:118-196 / :214-286):
+//   out[m*K + k] = bias[k] + sum_{r,s,c} X[n, oy*sh + r*dh - ph, ox*sw + s*dw - pw, c] * W[k,r,s,c]
+// with padding taps contributing nothing (here: zero-filled by TMA).
+//
+// B200 design (one persistent CTA per SM, 6 warps):
+//   warp 0     TMA producer.  Activations come through an im2col tensor map
+//              (padding, stride and dilation are done by the TMA unit:
+//              bounding-box corners, traversal strides, per-tap offsets),
+//              filters through a tiled map over W viewed as [K][R*S][C].
+//              Tiles land swizzled (SW128/64/32 for 128/64/32-byte channel
+//              blocks) in mbarrier-guarded rings.
+//   warp 1     MMA issuer: tcgen05.mma.cta_group::1.kind::i8, M=128, N=BN,
+//              K=32 bytes per instruction, int32 accumulators in TMEM.  Two
+//              accumulator buffers let the epilogue of tile i overlap the
+//              mainloop of tile i+1.
+//   warps 2-5  epilogue: tcgen05.ld (one output pixel per thread), + bias,
+//              16-byte int32 stores of the NHWK output.
+//
+// GENERIC: per k-block (tap r,s x channel block) one A tile of 128 output
+//   pixels and one B tile.
+// STRIP (stride_w = dilation_w = 1): the M dimension runs over padded-row
+//   positions (n, oy, j), j < Wp = out_w + S - 1.  Per (r, channel block) ONE
+//   im2col load of 128 + S - 1 consecutive positions feeds all S filter
+//   columns: the A descriptor of column s starts s rows later in the same
+//   swizzled strip (the swizzle follows absolute shared-memory address bits,
+//   so a whole-row shift needs no re-layout).  Positions j >= out_w are
+//   computed and dropped by the epilogue.  The reference reused a 130-pixel
+//   strip across the 3 filter columns the same way (spatial_strip.cuh:17-29,
+//   :98-116), for out_w % 128 == 0 only.
+// The reference's odd-K epilogue bug (generic_implicit_gemm.cuh:218-225) has
+// no counterpart: every column < K is stored.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "conv_common.h"
+#include "launch.h"
+#include "sm100.cuh"
+
+namespace i8c {
+
+template <int CBLK>
+struct SwizzleOf;
+template <>
+struct SwizzleOf<128> {
+  static constexpr Layout kLayout = Layout::kSw128;
+};
+template <>
+struct SwizzleOf<64> {
+  static constexpr Layout kLayout = Layout::kSw64;
+};
+template <>
+struct SwizzleOf<32> {
+  static constexpr Layout kLayout = Layout::kSw32;
+};
+
+// Shared-memory plan, identical on host and device.
+struct SmemPlan {
+  uint32_t a_bytes, b_bytes;  // one stage of A / B
+  uint32_t a_off, b_off, bar_off;
+  uint32_t total;             // bytes requested at launch (incl. alignment slack)
+};
+
+__host__ __device__ inline SmemPlan smem_plan(int cblk, int bn, int a_rows, int a_stages,
+                                              int b_stages) {
+  SmemPlan p;
+  p.a_bytes = a_rows * cblk;
+  p.b_bytes = bn * cblk;
+  p.a_off = 0;
+  p.b_off = p.a_off + a_stages * p.a_bytes;
+  p.bar_off = p.b_off + b_stages * p.b_bytes;
+  // a_full/a_empty[a_stages], b_full/b_empty[b_stages], tfull[2], tempty[2], drain, slot
+  const uint32_t bar_bytes = (2 * a_stages + 2 * b_stages + 5) * 8 + 8;
+  p.total = 1024 + p.bar_off + bar_bytes;
+  return p;
+}
+
+// Ring position: stage index and the parity of its current fill.
+struct Ring {
+  int stage = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next(int stages) {
+    if (++stage == stages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+  __device__ __forceinline__ void prev(int stages) {
+    if (--stage < 0) {
+      stage = stages - 1;
+      phase ^= 1u;
+    }
+  }
+};
+
+template <int CBLK, bool STRIP>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                const __grid_constant__ CUtensorMap tmap_w, const ConvGeom g,
+                const int32_t *__restrict__ bias, int32_t *__restrict__ out, const RunCtl ctl) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment: the SW128 atom (8 rows x 128 B) starts on it.
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int a_stages = STRIP ? g.a_stages : g.stages;
+  const int a_rows = STRIP ? g.a_rows : kBlockM;
+  const SmemPlan plan = smem_plan(CBLK, g.bn, a_rows, a_stages, g.stages);
+  uint8_t *a_ring = smem + plan.a_off;
+  uint8_t *b_ring = smem + plan.b_off;
+  uint64_t *a_full = reinterpret_cast<uint64_t *>(smem + plan.bar_off);
+  uint64_t *a_empty = a_full + a_stages;
+  uint64_t *b_full = a_empty + a_stages;
+  uint64_t *b_empty = b_full + g.stages;
+  uint64_t *tfull = b_empty + g.stages;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const WaitCtx wctx{ctl.wait_ns, ctl.status};
+  const int m_span = STRIP ? g.PWp : g.PQ;     // positions per image
+  const int m_row = STRIP ? g.Wp : g.Q;        // positions per output row
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a_stages; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < g.stages; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4 * 32);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, g.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      Ring ra, rb;
+      long issued_a = 0, issued_b = 0;
+      const uint32_t a_tx = (STRIP ? g.strip_px : kBlockM) * CBLK;
+      const uint32_t b_tx = plan.b_bytes;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < g.num_tiles && ok; tile += gridDim.x) {
+        const int m_tile = tile / g.n_tiles;
+        const int n_tile = tile - m_tile * g.n_tiles;
+        const int m0 = m_tile * kBlockM;
+        const int n0 = n_tile * g.bn;
+        const int img = m0 / m_span;
+        const int rem = m0 - img * m_span;
+        const int p = rem / m_row;
+        const int q = rem - p * m_row;
+        const int x_w = q * g.stride_w - g.pad_w;
+        const int x_h = p * g.stride_h - g.pad_h;
+        if constexpr (STRIP) {
+          for (int r = 0; r < g.R && ok; ++r) {
+            for (int cb = 0; cb < g.cblocks && ok; ++cb) {
+              if (!mbar_wait(&a_empty[ra.stage], ra.phase ^ 1u, wctx, kStatusTimeoutEmpty)) {
+                ok = false;
+                break;
+              }
+              if (!ctl.starve) {
+                mbar_arrive_expect_tx(&a_full[ra.stage], a_tx);
+                tma_load_im2col_4d(a_ring + ra.stage * plan.a_bytes, &tmap_x, &a_full[ra.stage],
+                                   cb * CBLK, x_w, x_h, img, 0,
+                                   static_cast<uint16_t>(r * g.dil_h));
+                ++issued_a;
+              }
+              ra.next(a_stages);
+              for (int s = 0; s < g.S; ++s) {
+                if (!mbar_wait(&b_empty[rb.stage], rb.phase ^ 1u, wctx, kStatusTimeoutEmpty)) {
+                  ok = false;
+                  break;
+                }
+                if (!ctl.starve) {
+                  mbar_arrive_expect_tx(&b_full[rb.stage], b_tx);
+                  tma_load_3d(b_ring + rb.stage * plan.b_bytes, &tmap_w, &b_full[rb.stage],
+                              cb * CBLK, r * g.S + s, n0);
+                  ++issued_b;
+                }
+                rb.next(g.stages);
+              }
+            }
+          }
+        } else {
+          int tap = 0, cb = 0, r = 0, s = 0;
+          for (int kb = 0; kb < g.kblocks; ++kb) {
+            if (!mbar_wait(&b_empty[rb.stage], rb.phase ^ 1u, wctx, kStatusTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            if (!ctl.starve) {
+              // A and B of one k-block share a stage index and one barrier.
+              mbar_arrive_expect_tx(&b_full[rb.stage], a_tx + b_tx);
+              tma_load_im2col_4d(a_ring + rb.stage * plan.a_bytes, &tmap_x, &b_full[rb.stage],
+                                 cb * CBLK, x_w, x_h, img, static_cast<uint16_t>(s * g.dil_w),
+                                 static_cast<uint16_t>(r * g.dil_h));
+              tma_load_3d(b_ring + rb.stage * plan.b_bytes, &tmap_w, &b_full[rb.stage], cb * CBLK,
+                          tap, n0);
+              ++issued_b;
+            }
+            rb.next(g.stages);
+            if (++cb == g.cblocks) {
+              cb = 0;
+              ++tap;
+              if (++s == g.S) {
+                s = 0;
+                ++r;
+              }
+            }
+          }
+        }
+      }
+      // Copies still in flight must land before the CTA exits: wait for the
+      // fills this thread armed most recently (immediate on the normal path).
+      for (long i = 0, n = issued_b < g.stages ? issued_b : g.stages; i < n; ++i) {
+        rb.prev(g.stages);
+        mbar_wait(&b_full[rb.stage], rb.phase, wctx, kStatusTimeoutTeardown);
+      }
+      for (long i = 0, n = issued_a < a_stages ? issued_a : a_stages; i < n; ++i) {
+        ra.prev(a_stages);
+        mbar_wait(&a_full[ra.stage], ra.phase, wctx, kStatusTimeoutTeardown);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_s8(kBlockM, g.bn);
+      constexpr Layout kLayout = SwizzleOf<CBLK>::kLayout;
+      constexpr uint32_t kAtom = 8 * CBLK;  // 8 rows x CBLK bytes
+      Ring ra, rb;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < g.num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, wctx, kStatusTimeoutDrain)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * g.acc_stride);
+        uint32_t accumulate = 0;
+        if constexpr (STRIP) {
+          for (int rc = 0; rc < g.R * g.cblocks && ok; ++rc) {
+            if (!mbar_wait(&a_full[ra.stage], ra.phase, wctx, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            const uint32_t a_addr = smem_u32(a_ring + ra.stage * plan.a_bytes);
+            for (int s = 0; s < g.S; ++s) {
+              if (!mbar_wait(&b_full[rb.stage], rb.phase, wctx, kStatusTimeoutFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t b_addr = smem_u32(b_ring + rb.stage * plan.b_bytes);
+#pragma unroll
+              for (int k = 0; k < CBLK / 32; ++k) {
+                // Filter column s reads the strip s rows further on.
+                const uint64_t a_desc =
+                    smem_desc(a_addr + s * CBLK + 32 * k, 16, kAtom, kLayout);
+                const uint64_t b_desc = smem_desc(b_addr + 32 * k, 16, kAtom, kLayout);
+                umma_i8(d_tmem, a_desc, b_desc, idesc, accumulate);
+                accumulate = 1;
+              }
+              umma_commit(&b_empty[rb.stage]);
+              rb.next(g.stages);
+            }
+            if (!ok) break;
+            umma_commit(&a_empty[ra.stage]);
+            ra.next(a_stages);
+          }
+        } else {
+          for (int kb = 0; kb < g.kblocks; ++kb) {
+            if (!mbar_wait(&b_full[rb.stage], rb.phase, wctx, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(a_ring + rb.stage * plan.a_bytes);
+            const uint32_t b_addr = smem_u32(b_ring + rb.stage * plan.b_bytes);
+#pragma unroll
+            for (int k = 0; k < CBLK / 32; ++k) {
+              const uint64_t a_desc = smem_desc(a_addr + 32 * k, 16, kAtom, kLayout);
+              const uint64_t b_desc = smem_desc(b_addr + 32 * k, 16, kAtom, kLayout);
+              umma_i8(d_tmem, a_desc, b_desc, idesc, accumulate);
+              accumulate = 1;
+            }
+            umma_commit(&b_empty[rb.stage]);
+            rb.next(g.stages);
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA issued must finish before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, wctx, kStatusTimeoutTeardown);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const bool vec_k = (g.K & 3) == 0;
+    const int m_limit = STRIP ? g.Mp : g.M;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < g.num_tiles; tile += gridDim.x) {
+      const int m_tile = tile / g.n_tiles;
+      const int n_tile = tile - m_tile * g.n_tiles;
+      const int pos = m_tile * kBlockM + row;
+      const int n0 = n_tile * g.bn;
+      bool valid = pos < m_limit;
+      int m = pos;
+      if constexpr (STRIP) {
+        const int img = pos / g.PWp;
+        const int rem = pos - img * g.PWp;
+        const int p = rem / g.Wp;
+        const int j = rem - p * g.Wp;
+        valid = valid && j < g.Q;
+        m = (img * g.P + p) * g.Q + j;
+      }
+      // All lanes wait; the vote keeps the warp converged for tcgen05.ld even
+      // if the wait runs out on some lanes only.
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, wctx, kStatusTimeoutAccum)))
+        break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * g.acc_stride;
+      int32_t *dst_row = out + static_cast<int64_t>(m) * g.K + n0;
+      for (int c0 = 0; c0 < g.bn; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + c0, v);
+        tmem_ld_wait();
+        if (valid) {
+          const int col0 = n0 + c0;
+          if (vec_k && c0 + 32 <= g.bn && col0 + 32 <= g.K) {
+            const int4 *b4 = reinterpret_cast<const int4 *>(bias + col0);
+            int4 *d4 = reinterpret_cast<int4 *>(dst_row + c0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int4 bb = __ldg(b4 + j);
+              int4 o;
+              o.x = static_cast<int32_t>(v[4 * j + 0]) + bb.x;
+              o.y = static_cast<int32_t>(v[4 * j + 1]) + bb.y;
+              o.z = static_cast<int32_t>(v[4 * j + 2]) + bb.z;
+              o.w = static_cast<int32_t>(v[4 * j + 3]) + bb.w;
+              d4[j] = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (c0 + j < g.bn && col0 + j < g.K)
+                dst_row[c0 + j] = static_cast<int32_t>(v[j]) + __ldg(bias + col0 + j);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, g.tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+static int pick_cblk(int c) {
+  if (c % 128 == 0) return 128;
+  if (c % 64 == 0) return 64;
+  return 32;
+}
+
+static int pick_bn(int k) {
+  if (k <= 256) return (k + 15) / 16 * 16;
+  // Balance the N tiles: the smallest multiple of 16 giving ceil(k/256) tiles.
+  const int tiles = (k + 255) / 256;
+  const int per = (k + tiles - 1) / tiles;
+  return (per + 15) / 16 * 16;
+}
+
+static int next_pow2(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+// Fills the launch geometry; false if the shape does not fit the kernel.
+static bool plan_geometry(const int8conv_shape &s, bool strip, ConvGeom &g, int &cblk) {
+  const int32_t out_h = (s.h + 2 * s.pad_h - s.dilation_h * (s.r - 1) - 1) / s.stride_h + 1;
+  const int32_t out_w = (s.w + 2 * s.pad_w - s.dilation_w * (s.s - 1) - 1) / s.stride_w + 1;
+  cblk = pick_cblk(s.c);
+  g = ConvGeom{};
+  g.M = s.n * out_h * out_w;
+  g.K = s.k;
+  g.P = out_h;
+  g.Q = out_w;
+  g.PQ = out_h * out_w;
+  g.R = s.r;
+  g.S = s.s;
+  g.pad_h = s.pad_h;
+  g.pad_w = s.pad_w;
+  g.stride_h = s.stride_h;
+  g.stride_w = s.stride_w;
+  g.dil_h = s.dilation_h;
+  g.dil_w = s.dilation_w;
+  g.cblocks = (s.c + cblk - 1) / cblk;
+  g.kblocks = s.r * s.s * g.cblocks;
+  g.bn = pick_bn(s.k);
+  g.acc_stride = (g.bn + 31) / 32 * 32;
+  g.tmem_cols = next_pow2(2 * g.acc_stride);
+  if (g.tmem_cols > 512) return false;
+  const int b_bytes = g.bn * cblk;
+  const int budget = kMaxSmem - 1024 - 512;
+  if (strip) {
+    g.Wp = out_w + s.s - 1;
+    g.PWp = out_h * g.Wp;
+    const int64_t mp = static_cast<int64_t>(s.n) * g.PWp;
+    if (mp >= (int64_t(1) << 31)) return false;
+    g.Mp = static_cast<int32_t>(mp);
+    g.strip_px = kBlockM + s.s - 1;
+    g.a_rows = (g.strip_px + 7) / 8 * 8;
+    const int a_bytes = g.a_rows * cblk;
+    // Strip ring: enough strips to keep S filter tiles per strip flowing.
+    g.a_stages = 3;
+    int b_stages = (budget - g.a_stages * a_bytes) / b_bytes;
+    if (b_stages > 8) b_stages = 8;
+    if (b_stages < 2) {
+      g.a_stages = 2;
+      b_stages = (budget - g.a_stages * a_bytes) / b_bytes;
+      if (b_stages > 8) b_stages = 8;
+    }
+    if (b_stages < 2) return false;
+    g.stages = b_stages;
+    g.m_tiles = (g.Mp + kBlockM - 1) / kBlockM;
+  } else {
+    const int per_stage = kBlockM * cblk + b_bytes;
+    int stages = budget / per_stage;
+    if (stages > 8) stages = 8;
+    if (stages < 2) return false;
+    g.stages = stages;
+    g.a_stages = stages;
+    g.a_rows = kBlockM;
+    g.m_tiles = (g.M + kBlockM - 1) / kBlockM;
+  }
+  g.n_tiles = (s.k + g.bn - 1) / g.bn;
+  g.num_tiles = g.m_tiles * g.n_tiles;
+  return true;
+}
+
+template <int CBLK, bool STRIP>
+static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, const int8_t *x,
+                                const int8_t *w, const int32_t *b, int32_t *y,
+                                cudaStream_t stream) {
+  DeviceInfo &dev = device_info();
+  CUtensorMap maps[2];
+  const int pixels = STRIP ? g.strip_px : kBlockM;
+  const int count_w = STRIP ? g.Wp : g.Q;
+  int8conv_status st = activation_map_im2col(s, x, CBLK, pixels, count_w, &maps[0]);
+  if (st != INT8CONV_OK) return st;
+  st = filter_map_tiled(s, w, CBLK, g.bn, &maps[1]);
+  if (st != INT8CONV_OK) return st;
+  const SmemPlan plan =
+      smem_plan(CBLK, g.bn, STRIP ? g.a_rows : kBlockM, g.a_stages, g.stages);
+  auto kernel = conv_kernel<CBLK, STRIP>;
+  if (!ensure_smem_attr(reinterpret_cast<const void *>(kernel), plan.total))
+    return INT8CONV_CUDA_ERROR;
+  const int grid = g.num_tiles < dev.sm_count ? g.num_tiles : dev.sm_count;
+  kernel<<<grid, kThreads, plan.total, stream>>>(maps[0], maps[1], g, b, y, run_ctl());
+  note_launch();
+  return cudaGetLastError() == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
+}
+
+template <bool STRIP>
+static int8conv_status launch_family(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                     const int32_t *b, int32_t *y, cudaStream_t stream) {
+  ConvGeom g;
+  int cblk = 0;
+  if (!plan_geometry(s, STRIP, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+  switch (cblk) {
+    case 128:
+      return launch_t<128, STRIP>(s, g, x, w, b, y, stream);
+    case 64:
+      return launch_t<64, STRIP>(s, g, x, w, b, y, stream);
+    default:
+      return launch_t<32, STRIP>(s, g, x, w, b, y, stream);
+  }
+}
+
+int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                    const int32_t *b, int32_t *y, cudaStream_t stream) {
+  return launch_family<false>(s, x, w, b, y, stream);
+}
+
+int8conv_status launch_strip_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                  const int32_t *b, int32_t *y, cudaStream_t stream) {
+  return launch_family<true>(s, x, w, b, y, stream);
+}
+
+}  // namespace i8c

@@ -1,0 +1,394 @@
+// conv_lab.cpp - the lab's command-line harness, over the C ABI.
+//
+// Mirrors src/conv_lab.cu of pthodima/int8_kernel_lab:
+//   * same flags: --strategy, --csv, --warmup N (20), --iterations N (101)
+//     (conv_lab.cu:112-145), plus --case/--config to pick a workloads.csv row
+//     at run time (the reference compiles one binary per case), --values,
+//     --seed, --batch, --peak-tops, --no-graph;
+//   * same flow: seeded inputs, device buffers, launch, validate before
+//     timing, per-launch event median (conv_lab.cu:88-110), winner, CSV or
+//     human line, exit code 0 only if every run was correct and one ran
+//     (conv_lab.cu:241);
+//   * same first 16 CSV columns in the same order (conv_lab.cu:223-230), then
+//     the appended ones: eligible_halo, eligible_splitk, halo_ms, splitk_ms,
+//     halo_correct, splitk_correct, gpus, tops, roofline_frac, oracle_ms,
+//     oracle_threads, graph_ms.
+// Validation compares EVERY output element (the reference checks 2048
+// strided samples above 65536 outputs, conv_lab.cu:72-77) against a direct
+// host convolution with the loop nest of conv_lab.cu:39-66.
+// --strategy both = generic + strip (as in the reference); all = the four
+// families; auto = the dispatch policy's pick; or one family name.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <fstream>
+#include <iomanip>
+#include <iostream>
+#include <random>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "int8conv.h"
+
+namespace {
+
+void check(cudaError_t status, const char *what) {
+  if (status != cudaSuccess) {
+    std::cerr << what << ": " << cudaGetErrorString(status) << '\n';
+    std::exit(EXIT_FAILURE);
+  }
+}
+
+template <class T>
+class DeviceBuffer {
+ public:
+  explicit DeviceBuffer(size_t elements) {
+    check(cudaMalloc(&data_, std::max<size_t>(elements, 1) * sizeof(T)), "cudaMalloc");
+  }
+  ~DeviceBuffer() { cudaFree(data_); }
+  T *get() { return data_; }
+  DeviceBuffer(const DeviceBuffer &) = delete;
+  DeviceBuffer &operator=(const DeviceBuffer &) = delete;
+
+ private:
+  T *data_ = nullptr;
+};
+
+struct Options {
+  std::string strategy = "both";
+  bool csv = false;
+  int warmup = 20;
+  int iterations = 101;
+  std::string case_name = "smoke";
+  std::string config;
+  std::string values = "full";
+  uint32_t seed = 20260925;
+  int batch = 0;
+  double peak_tops = 4500.0;
+  bool graph = true;
+};
+
+[[noreturn]] void usage() {
+  std::cerr << "usage: conv_lab [--strategy generic|strip|halo|splitk|both|all|auto] [--csv] "
+               "[--warmup N] [--iterations N] [--case NAME] [--config CSV] "
+               "[--values full|reference] [--seed S] [--batch N] [--peak-tops T] "
+               "[--no-graph]\n";
+  std::exit(EXIT_FAILURE);
+}
+
+Options parse_options(int argc, char **argv) {
+  Options o;
+  for (int i = 1; i < argc; ++i) {
+    const std::string arg = argv[i];
+    auto value = [&]() -> std::string {
+      if (i + 1 >= argc) usage();
+      return argv[++i];
+    };
+    if (arg == "--csv") o.csv = true;
+    else if (arg == "--no-graph") o.graph = false;
+    else if (arg == "--strategy") o.strategy = value();
+    else if (arg == "--warmup") o.warmup = std::stoi(value());
+    else if (arg == "--iterations") o.iterations = std::stoi(value());
+    else if (arg == "--case") o.case_name = value();
+    else if (arg == "--config") o.config = value();
+    else if (arg == "--values") o.values = value();
+    else if (arg == "--seed") o.seed = static_cast<uint32_t>(std::stoul(value()));
+    else if (arg == "--batch") o.batch = std::stoi(value());
+    else if (arg == "--peak-tops") o.peak_tops = std::stod(value());
+    else usage();
+  }
+  const std::vector<std::string> ok = {"generic", "strip", "halo", "splitk", "both", "all", "auto"};
+  if (std::find(ok.begin(), ok.end(), o.strategy) == ok.end() || o.warmup < 0 ||
+      o.iterations <= 0 || (o.values != "full" && o.values != "reference") || o.batch < 0) {
+    std::cerr << "invalid benchmark options\n";
+    std::exit(EXIT_FAILURE);
+  }
+  return o;
+}
+
+std::string default_config(const char *argv0) {
+  // lib/conv_lab -> ../workloads.csv
+  std::string self = argv0;
+  const size_t slash = self.find_last_of('/');
+  const std::string dir = slash == std::string::npos ? "." : self.substr(0, slash);
+  return dir + "/../workloads.csv";
+}
+
+bool load_case(const std::string &path, const std::string &name, int8conv_shape &shape) {
+  std::ifstream file(path);
+  if (!file) return false;
+  std::string line;
+  std::getline(file, line);  // header: name,n,h,w,c,k,r,s,pad_h,pad_w,stride_h,stride_w,dilation_h,dilation_w
+  while (std::getline(file, line)) {
+    std::stringstream ss(line);
+    std::string cell;
+    std::getline(ss, cell, ',');
+    if (cell != name) continue;
+    int32_t v[13];
+    for (int i = 0; i < 13; ++i) {
+      if (!std::getline(ss, cell, ',')) return false;
+      v[i] = std::stoi(cell);
+    }
+    shape = int8conv_shape{v[0], v[1], v[2], v[3], v[4], v[5], v[6],
+                           v[7], v[8], v[9], v[10], v[11], v[12]};
+    return true;
+  }
+  return false;
+}
+
+// Every output element against a direct host convolution: the loop nest of
+// the reference's reference_value (conv_lab.cu:39-66), all outputs, threaded.
+bool validate_all(const int8conv_shape &s, const int8conv_dims &d,
+                  const std::vector<int8_t> &x, const std::vector<int8_t> &w,
+                  const std::vector<int32_t> &b, const std::vector<int32_t> &y,
+                  const char *label, int threads, double &ms) {
+  const auto t0 = std::chrono::steady_clock::now();
+  std::vector<long long> first_bad(threads, -1);
+  std::vector<std::thread> pool;
+  for (int t = 0; t < threads; ++t) {
+    pool.emplace_back([&, t] {
+      for (int64_t m = t; m < d.gemm_m; m += threads) {
+        const int ox = static_cast<int>(m % d.out_w);
+        const int oy = static_cast<int>((m / d.out_w) % d.out_h);
+        const int64_t n = m / (static_cast<int64_t>(d.out_w) * d.out_h);
+        for (int k = 0; k < s.k; ++k) {
+          int32_t sum = b[k];
+          for (int fy = 0; fy < s.r; ++fy) {
+            const int iy = oy * s.stride_h + fy * s.dilation_h - s.pad_h;
+            if (iy < 0 || iy >= s.h) continue;
+            for (int fx = 0; fx < s.s; ++fx) {
+              const int ix = ox * s.stride_w + fx * s.dilation_w - s.pad_w;
+              if (ix < 0 || ix >= s.w) continue;
+              const int8_t *xp = &x[((n * s.h + iy) * s.w + ix) * s.c];
+              const int8_t *wp = &w[((static_cast<int64_t>(k) * s.r + fy) * s.s + fx) * s.c];
+              for (int c = 0; c < s.c; ++c) sum += int32_t(xp[c]) * int32_t(wp[c]);
+            }
+          }
+          if (y[m * s.k + k] != sum) {
+            first_bad[t] = m * s.k + k;
+            return;
+          }
+        }
+      }
+    });
+  }
+  for (auto &th : pool) th.join();
+  ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  for (long long idx : first_bad) {
+    if (idx >= 0) {
+      std::cerr << label << " mismatch at output " << idx << ": got " << y[idx] << '\n';
+      return false;
+    }
+  }
+  return true;
+}
+
+template <class Function>
+float measure(Function launch, int warmup, int iterations) {
+  for (int i = 0; i < warmup; ++i) launch();
+  check(cudaDeviceSynchronize(), "warmup");
+  std::vector<float> samples;
+  samples.reserve(iterations);
+  cudaEvent_t start, stop;
+  check(cudaEventCreate(&start), "cudaEventCreate start");
+  check(cudaEventCreate(&stop), "cudaEventCreate stop");
+  for (int i = 0; i < iterations; ++i) {
+    check(cudaEventRecord(start), "cudaEventRecord start");
+    launch();
+    check(cudaEventRecord(stop), "cudaEventRecord stop");
+    check(cudaEventSynchronize(stop), "cudaEventSynchronize");
+    float ms = 0;
+    check(cudaEventElapsedTime(&ms, start, stop), "cudaEventElapsedTime");
+    samples.push_back(ms);
+  }
+  cudaEventDestroy(start);
+  cudaEventDestroy(stop);
+  std::sort(samples.begin(), samples.end());
+  return samples[samples.size() / 2];
+}
+
+// Launch time amortised over a CUDA graph of `count` back-to-back launches.
+template <class Function>
+float measure_graph(Function launch, int count, int replays) {
+  cudaStream_t stream;
+  check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+  cudaGraph_t graph;
+  cudaGraphExec_t exec;
+  check(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "capture");
+  for (int i = 0; i < count; ++i) launch(stream);
+  check(cudaStreamEndCapture(stream, &graph), "end capture");
+  check(cudaGraphInstantiate(&exec, graph, 0), "instantiate");
+  check(cudaGraphLaunch(exec, stream), "graph warmup");
+  check(cudaStreamSynchronize(stream), "graph sync");
+  cudaEvent_t start, stop;
+  check(cudaEventCreate(&start), "event");
+  check(cudaEventCreate(&stop), "event");
+  std::vector<float> samples;
+  for (int r = 0; r < replays; ++r) {
+    check(cudaEventRecord(start, stream), "record");
+    check(cudaGraphLaunch(exec, stream), "graph launch");
+    check(cudaEventRecord(stop, stream), "record");
+    check(cudaEventSynchronize(stop), "sync");
+    float ms = 0;
+    check(cudaEventElapsedTime(&ms, start, stop), "elapsed");
+    samples.push_back(ms / count);
+  }
+  std::sort(samples.begin(), samples.end());
+  cudaEventDestroy(start);
+  cudaEventDestroy(stop);
+  cudaGraphExecDestroy(exec);
+  cudaGraphDestroy(graph);
+  cudaStreamDestroy(stream);
+  return samples[samples.size() / 2];
+}
+
+std::string fmt(double v) {
+  std::ostringstream os;
+  os << v;
+  return os.str();
+}
+
+}  // namespace
+
+int main(int argc, char **argv) {
+  const Options options = parse_options(argc, argv);
+  const std::string config = options.config.empty() ? default_config(argv[0]) : options.config;
+  int8conv_shape shape;
+  if (!load_case(config, options.case_name, shape)) {
+    std::cerr << "unknown case " << options.case_name << " in " << config << '\n';
+    return EXIT_FAILURE;
+  }
+  if (options.batch > 0) shape.n = options.batch;
+  int8conv_dims d;
+  if (int8conv_shape_dims(&shape, &d) != INT8CONV_OK) {
+    std::cerr << "invalid shape for case " << options.case_name << '\n';
+    return EXIT_FAILURE;
+  }
+
+  // Seeded host inputs (conv_lab.cu:149-157); --values full uses the whole
+  // int8 range and a bias in [-65536, 65536].
+  std::mt19937 rng(options.seed);
+  const bool ref_values = options.values == "reference";
+  std::uniform_int_distribution<int> values(ref_values ? -4 : -128, ref_values ? 4 : 127);
+  std::uniform_int_distribution<int> bias_values(ref_values ? -31 : -65536,
+                                                 ref_values ? 31 : 65536);
+  std::vector<int8_t> input(d.input_elements), filter(d.filter_elements);
+  std::vector<int32_t> bias(shape.k);
+  for (auto &v : input) v = static_cast<int8_t>(values(rng));
+  for (auto &v : filter) v = static_cast<int8_t>(values(rng));
+  for (auto &v : bias) v = bias_values(rng);
+
+  DeviceBuffer<int8_t> d_input(input.size());
+  DeviceBuffer<int8_t> d_filter(filter.size());
+  DeviceBuffer<int32_t> d_bias(bias.size());
+  DeviceBuffer<int32_t> d_output(d.output_elements);
+  check(cudaMemcpy(d_input.get(), input.data(), input.size(), cudaMemcpyHostToDevice), "copy input");
+  check(cudaMemcpy(d_filter.get(), filter.data(), filter.size(), cudaMemcpyHostToDevice),
+        "copy filter");
+  check(cudaMemcpy(d_bias.get(), bias.data(), bias.size() * sizeof(int32_t),
+                   cudaMemcpyHostToDevice),
+        "copy bias");
+
+  // Families to run.
+  bool run[INT8CONV_NUM_STRATEGIES] = {false, false, false, false};
+  if (options.strategy == "both") run[INT8CONV_GENERIC] = run[INT8CONV_STRIP] = true;
+  else if (options.strategy == "all") std::fill(run, run + INT8CONV_NUM_STRATEGIES, true);
+  else if (options.strategy == "auto") run[int8conv_select(&shape)] = true;
+  else {
+    for (int f = 0; f < INT8CONV_NUM_STRATEGIES; ++f)
+      if (options.strategy == int8conv_strategy_name(f)) run[f] = true;
+  }
+  bool eligible[INT8CONV_NUM_STRATEGIES];
+  float ms[INT8CONV_NUM_STRATEGIES], graph_ms[INT8CONV_NUM_STRATEGIES];
+  bool correct[INT8CONV_NUM_STRATEGIES];
+  double oracle_ms = 0;
+  const int threads = std::max(1u, std::thread::hardware_concurrency());
+  std::vector<int32_t> output(d.output_elements);
+  for (int f = 0; f < INT8CONV_NUM_STRATEGIES; ++f) {
+    eligible[f] = int8conv_eligible(&shape, f) != 0;
+    ms[f] = -1.0f;
+    graph_ms[f] = -1.0f;
+    correct[f] = true;
+    if (!run[f] || !eligible[f]) continue;
+    const size_t ws_bytes = int8conv_workspace_bytes(&shape, f);
+    DeviceBuffer<uint8_t> workspace(ws_bytes);
+    auto launch_on = [&](cudaStream_t stream) {
+      const int8conv_status st =
+          int8conv_launch(f, &shape, d_input.get(), d_filter.get(), d_bias.get(),
+                          d_output.get(), workspace.get(), ws_bytes, stream);
+      if (st != INT8CONV_OK) {
+        std::cerr << int8conv_strategy_name(f) << " launch: " << int8conv_status_string(st)
+                  << '\n';
+        std::exit(EXIT_FAILURE);
+      }
+    };
+    auto launch = [&] { launch_on(nullptr); };
+    check(cudaMemset(d_output.get(), 0xA5, d.output_elements * sizeof(int32_t)), "poison");
+    launch();
+    check(cudaGetLastError(), "launch");
+    check(cudaDeviceSynchronize(), "synchronize");
+    if (int8conv_device_status() != INT8CONV_OK) {
+      std::cerr << int8conv_strategy_name(f) << ": device wait timed out\n";
+      correct[f] = false;
+      continue;
+    }
+    check(cudaMemcpy(output.data(), d_output.get(), output.size() * sizeof(int32_t),
+                     cudaMemcpyDeviceToHost),
+          "copy output");
+    double vms = 0;
+    correct[f] = validate_all(shape, d, input, filter, bias, output,
+                              int8conv_strategy_name(f), threads, vms);
+    oracle_ms = std::max(oracle_ms, vms);
+    if (!correct[f]) continue;
+    ms[f] = measure(launch, options.warmup, options.iterations);
+    if (options.graph) graph_ms[f] = measure_graph(launch_on, 20, 11);
+  }
+
+  int winner = -1;
+  for (int f = 0; f < INT8CONV_NUM_STRATEGIES; ++f)
+    if (ms[f] >= 0 && (winner < 0 || ms[f] < ms[winner])) winner = f;
+  const char *winner_name = winner < 0 ? "none" : int8conv_strategy_name(winner);
+  const double ops = 2.0 * double(d.gemm_m) * double(d.gemm_n) * double(d.gemm_k);
+  const double tops = winner < 0 ? -1.0 : ops / (ms[winner] * 1e-3) / 1e12;
+  bool all_correct = true;
+  for (int f = 0; f < INT8CONV_NUM_STRATEGIES; ++f) all_correct = all_correct && correct[f];
+
+  if (options.csv) {
+    std::cout << "case,n,h,w,c,k,r,s,out_h,out_w,eligible_strip,generic_ms,strip_ms,winner,"
+                 "generic_correct,strip_correct,eligible_halo,eligible_splitk,halo_ms,splitk_ms,"
+                 "halo_correct,splitk_correct,gpus,tops,roofline_frac,oracle_ms,oracle_threads,"
+                 "graph_ms\n";
+    std::cout << options.case_name << ',' << shape.n << ',' << shape.h << ',' << shape.w << ','
+              << shape.c << ',' << shape.k << ',' << shape.r << ',' << shape.s << ',' << d.out_h
+              << ',' << d.out_w << ',' << (eligible[INT8CONV_STRIP] ? 1 : 0) << ','
+              << ms[INT8CONV_GENERIC] << ',' << ms[INT8CONV_STRIP] << ',' << winner_name << ','
+              << (correct[INT8CONV_GENERIC] ? 1 : 0) << ',' << (correct[INT8CONV_STRIP] ? 1 : 0)
+              << ',' << (eligible[INT8CONV_HALO] ? 1 : 0) << ','
+              << (eligible[INT8CONV_SPLITK] ? 1 : 0) << ',' << ms[INT8CONV_HALO] << ','
+              << ms[INT8CONV_SPLITK] << ',' << (correct[INT8CONV_HALO] ? 1 : 0) << ','
+              << (correct[INT8CONV_SPLITK] ? 1 : 0) << ",1," << fmt(tops) << ','
+              << fmt(tops < 0 ? -1.0 : tops / options.peak_tops) << ',' << fmt(oracle_ms) << ','
+              << threads << ',' << (winner < 0 ? -1.0f : graph_ms[winner]) << '\n';
+  } else {
+    std::cout << options.case_name << ":";
+    for (int f = 0; f < INT8CONV_NUM_STRATEGIES; ++f) {
+      std::cout << ' ' << int8conv_strategy_name(f) << ' ';
+      if (!eligible[f]) std::cout << "ineligible";
+      else if (!run[f]) std::cout << "not run";
+      else if (ms[f] >= 0)
+        std::cout << std::fixed << std::setprecision(4) << ms[f] << " ms";
+      else std::cout << "failed";
+      std::cout << (f + 1 < INT8CONV_NUM_STRATEGIES ? "," : "");
+    }
+    std::cout << ", winner " << winner_name;
+    if (winner >= 0) std::cout << " (" << std::setprecision(1) << tops << " TOPS)";
+    std::cout << '\n';
+  }
+  return all_correct && winner >= 0 ? 0 : 1;
+}

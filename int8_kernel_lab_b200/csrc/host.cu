@@ -154,9 +154,32 @@ RunCtl run_ctl() {
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 bool ensure_smem_attr(const void *kernel, int bytes) {
-  // Idempotent and cheap; the runtime caches the attribute per function.
-  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
-         cudaSuccess;
+  // Remember the largest limit already set per (device, kernel).
+  struct Entry {
+    int device;
+    const void *kernel;
+    int bytes;
+  };
+  static Entry table[256];
+  static int used = 0;
+  static std::mutex mutex;
+  const int dev = device_info().device;
+  std::lock_guard<std::mutex> lock(mutex);
+  for (int i = 0; i < used; ++i) {
+    if (table[i].device == dev && table[i].kernel == kernel) {
+      if (table[i].bytes >= bytes) return true;
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+          cudaSuccess)
+        return false;
+      table[i].bytes = bytes;
+      return true;
+    }
+  }
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess)
+    return false;
+  if (used < 256) table[used++] = Entry{dev, kernel, bytes};
+  return true;
 }
 
 int8conv_status activation_map_im2col(const int8conv_shape &s, const int8_t *x, int channels,

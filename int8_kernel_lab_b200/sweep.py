@@ -1,0 +1,66 @@
+#!/usr/bin/env python3
+"""Measure a set of workloads with the conv_lab CLI and write one CSV row each.
+
+B200 counterpart of the reference's scripts/sweep.py (same flags where they
+apply: --configs, --cases, --output, --iterations).  Shapes are runtime
+arguments of one conv_lab binary, so there is no per-case rebuild (the
+reference ran `make CASE=...` per case, sweep.py:35-38).  Every eligible
+family is run (--strategy all); rows are written incrementally after each case
+(sweep.py:58-61), so an interrupted sweep keeps what it measured.  The CSV is
+conv_lab's: the reference's 16 columns, then the appended ones.
+
+    python -m int8_kernel_lab_b200.sweep --cases cfg2_mid_3x3,big_3x3_s1 \\
+        --output build/dispatch_measurements.csv
+"""
+import argparse
+import csv
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--configs", default=str(PKG / "workloads.csv"), type=Path)
+    ap.add_argument("--cases", help="comma-separated case names; default all")
+    ap.add_argument("--output", default="build/dispatch_measurements.csv", type=Path)
+    ap.add_argument("--iterations", type=int, default=101)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--strategy", default="all")
+    ap.add_argument("--values", default="full", choices=("full", "reference"))
+    ap.add_argument("--conv-lab", default=str(PKG / "lib" / "conv_lab"))
+    args = ap.parse_args(argv)
+    with open(args.configs, newline="") as stream:
+        rows = list(csv.DictReader(stream))
+    requested = args.cases.split(",") if args.cases else [r["name"] for r in rows]
+    unknown = sorted(set(requested) - {r["name"] for r in rows})
+    if unknown:
+        raise SystemExit(f"unknown cases: {', '.join(unknown)}")
+    args.output.parent.mkdir(parents=True, exist_ok=True)
+    measurements = []
+    status = 0
+    for case in requested:
+        result = subprocess.run(
+            [args.conv_lab, "--case", case, "--config", str(args.configs), "--strategy",
+             args.strategy, "--iterations", str(args.iterations), "--warmup", str(args.warmup),
+             "--values", args.values, "--csv"], text=True, capture_output=True)
+        if result.returncode != 0:
+            status = 1
+            sys.stderr.write(result.stderr)
+        lines = result.stdout.strip().splitlines()
+        if len(lines) < 2:
+            print(f"{case}: conv_lab failed (exit {result.returncode})", file=sys.stderr)
+            continue
+        measurements.append(next(csv.DictReader(lines)))
+        with open(args.output, "w", newline="") as stream:
+            writer = csv.DictWriter(stream, fieldnames=measurements[0].keys())
+            writer.writeheader()
+            writer.writerows(measurements)
+        print(f"{case}: wrote {args.output}", flush=True)
+    return status
+
+
+if __name__ == "__main__":
+    sys.exit(main())

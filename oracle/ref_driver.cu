@@ -6,11 +6,12 @@
 // the reference's own scripts/gen_case.py writes, and renames its main() so
 // this file can add two modes:
 //
-//   ref_<case> cpu IN.bin FILTER.bin BIAS.bin OUT.bin [m_begin m_end [threads]]
+//   ref_<case> cpu IN.bin FILTER.bin BIAS.bin OUT.bin [m_begin m_end [threads [steps]]]
 //       Computes output rows [m_begin, m_end) with the reference's CPU oracle
 //       reference_value<TestShape> (src/conv_lab.cu:39-66), called once per
 //       output element exactly as validate<Shape> does (conv_lab.cu:78), over
-//       `threads` OpenMP threads.  Prints one JSON line with the wall time.
+//       `threads` OpenMP threads, `steps` times (default 1).  Prints one JSON
+//       line with the wall time of every repetition.
 //   ref_<case> lab [conv_lab flags...]
 //       Runs the reference's own conv_lab main (src/conv_lab.cu:246-248):
 //       its mma.sync kernels built for this GPU, its validation and timing.
@@ -42,7 +43,7 @@ bool read_file(const char *path, std::vector<T> &data, size_t elements) {
 int cpu_mode(int argc, char **argv) {
   using Shape = TestShape;
   if (argc < 6) {
-    std::fprintf(stderr, "usage: %s cpu IN FILTER BIAS OUT [m_begin m_end [threads]]\n",
+    std::fprintf(stderr, "usage: %s cpu IN FILTER BIAS OUT [m_begin m_end [threads [steps]]]\n",
                  argv[0]);
     return 2;
   }
@@ -61,23 +62,28 @@ int cpu_mode(int argc, char **argv) {
     m_end = std::atoll(argv[7]);
   }
   if (argc >= 9) threads = std::atoi(argv[8]);
-  if (m_begin < 0 || m_end > Shape::gemm_m || m_begin > m_end || threads <= 0) {
+  int steps = 1;
+  if (argc >= 10) steps = std::atoi(argv[9]);
+  if (m_begin < 0 || m_end > Shape::gemm_m || m_begin > m_end || threads <= 0 || steps <= 0) {
     std::fprintf(stderr, "bad row range or thread count\n");
     return 2;
   }
   const size_t rows = static_cast<size_t>(m_end - m_begin);
   std::vector<int32_t> output(rows * Shape::k);
-  const auto start = std::chrono::steady_clock::now();
+  std::vector<double> seconds;
+  for (int step = 0; step < steps; ++step) {
+    const auto start = std::chrono::steady_clock::now();
 #pragma omp parallel for schedule(dynamic, 16) num_threads(threads)
-  for (long long m = m_begin; m < m_end; ++m) {
-    for (int k = 0; k < Shape::k; ++k) {
-      const size_t index = static_cast<size_t>(m) * Shape::k + k;
-      output[static_cast<size_t>(m - m_begin) * Shape::k + k] =
-          reference_value<Shape>(input, filter, bias, index);
+    for (long long m = m_begin; m < m_end; ++m) {
+      for (int k = 0; k < Shape::k; ++k) {
+        const size_t index = static_cast<size_t>(m) * Shape::k + k;
+        output[static_cast<size_t>(m - m_begin) * Shape::k + k] =
+            reference_value<Shape>(input, filter, bias, index);
+      }
     }
+    seconds.push_back(
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count());
   }
-  const double seconds =
-      std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
   std::ofstream out(argv[5], std::ios::binary);
   out.write(reinterpret_cast<const char *>(output.data()),
             static_cast<std::streamsize>(output.size() * sizeof(int32_t)));
@@ -85,11 +91,16 @@ int cpu_mode(int argc, char **argv) {
     std::fprintf(stderr, "cannot write %s\n", argv[5]);
     return 2;
   }
+  double total = 0;
+  for (double t : seconds) total += t;
   const double ops = 2.0 * static_cast<double>(rows) * Shape::k * Shape::r * Shape::s * Shape::c;
-  std::printf("{\"case\": \"%s\", \"rows\": %lld, \"threads\": %d, \"seconds\": %.6f, "
-              "\"gops\": %.3f}\n",
-              kCaseName, static_cast<long long>(rows), threads, seconds,
-              ops / seconds / 1e9);
+  std::printf("{\"case\": \"%s\", \"rows\": %lld, \"threads\": %d, \"steps\": %d, "
+              "\"seconds\": %.6f, \"gops\": %.3f, \"step_seconds\": [",
+              kCaseName, static_cast<long long>(rows), threads, steps, total / steps,
+              ops * steps / total / 1e9);
+  for (size_t i = 0; i < seconds.size(); ++i)
+    std::printf("%s%.6f", i ? ", " : "", seconds[i]);
+  std::printf("]}\n");
   return 0;
 }
 

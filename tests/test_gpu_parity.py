@@ -1,0 +1,208 @@
+"""GPU parity: every family against the CPU oracle, bit-exact, through the C ABI.
+
+Sizes are chosen so the oracle finishes in seconds; full-size BASELINE shapes
+are checked on every output of a few whole images plus a seeded random sample
+of all others (the oracle restates src/conv_lab.cu:39-66 of the reference).
+"""
+import numpy as np
+import pytest
+
+import pyoracle
+from conftest import golden_cases, load_golden
+
+import int8_kernel_lab_b200 as m
+from int8_kernel_lab_b200 import _abi
+
+pytestmark = pytest.mark.gpu
+
+FAMILIES = ("generic", "strip", "halo", "splitk")
+
+
+def _run(torch, strategy, shape, x, w, b):
+    dx = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    dw = torch.from_numpy(np.ascontiguousarray(w)).cuda()
+    db = torch.from_numpy(np.ascontiguousarray(b)).cuda()
+    # Poison the output so unwritten elements cannot pass by accident.
+    dy = torch.full((shape.output_elements,), -123456789, dtype=torch.int32, device="cuda")
+    nbytes = m.workspace_bytes(shape, strategy) if strategy != "auto" else 0
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device="cuda") if nbytes else None
+    m.launch(strategy, shape, dx, dw, db, dy, workspace=ws, workspace_bytes=nbytes)
+    assert m.device_status() == _abi.OK
+    return dy.cpu().numpy()
+
+
+def _families(shape):
+    return [f for f in FAMILIES if shape.eligible(f)]
+
+
+@pytest.mark.parametrize("name", golden_cases())
+def test_golden_fixtures_all_families(cuda, name):
+    shape, x, w, b, y = load_golden(name)
+    fams = _families(shape)
+    assert "generic" in fams
+    for fam in fams:
+        got = _run(cuda, fam, shape, x, w, b)
+        assert np.array_equal(got, y), f"{fam} differs from the reference on {name}"
+
+
+def _reduced(shape, max_ops=3e10):
+    if shape.ops <= max_ops:
+        return shape
+    return shape.with_batch(max(1, int(shape.n * max_ops / shape.ops)))
+
+
+@pytest.mark.parametrize("case", m.BASELINE_CASES)
+def test_baseline_configs_full_compare(cuda, case):
+    shape = _reduced(m.load_workloads()[case])
+    x, w, b = m.make_inputs(shape)
+    want = pyoracle.conv(shape, x, w, b)
+    for fam in _families(shape):
+        got = _run(cuda, fam, shape, x, w, b)
+        bad = np.count_nonzero(got != want)
+        assert bad == 0, f"{fam} on {case} (n={shape.n}): {bad} mismatches"
+
+
+def _sampled_check(shape, x, w, b, got, seed=7, samples=200_000, whole_images=(0, -1)):
+    """Every output of the listed images plus a random sample of all outputs."""
+    per_image = shape.out_h * shape.out_w
+    for img in whole_images:
+        img = img % shape.n
+        rows = pyoracle.conv_rows(shape, x, w, b, img * per_image, (img + 1) * per_image)
+        lo = img * per_image * shape.k
+        assert np.array_equal(got[lo:lo + rows.size], rows), f"image {img} differs"
+    rng = np.random.RandomState(seed)
+    idx = rng.randint(0, shape.output_elements, size=min(samples, shape.output_elements))
+    assert np.array_equal(got[idx], pyoracle.values(shape, x, w, b, idx))
+
+
+@pytest.mark.parametrize("case", ["cfg5a_stress_3x3", "cfg5b_dilated_3x3", "cfg5c_1x7",
+                                  "cfg2_mid_3x3", "cfg3b_pointwise"])
+def test_baseline_full_size_sampled(cuda, case):
+    shape = m.load_workloads()[case]
+    x, w, b = m.make_inputs(shape)
+    for fam in _families(shape):
+        got = _run(cuda, fam, shape, x, w, b)
+        _sampled_check(shape, x, w, b, got)
+
+
+def test_families_agree_bitwise_full_size(cuda):
+    # Size-independent property: every eligible family computes the same
+    # integers (order of the int32 reduction cannot matter: no overflow).
+    shape = m.load_workloads()["cfg5a_stress_3x3"]
+    x, w, b = m.make_inputs(shape, seed=99)
+    fams = _families(shape)
+    outs = [_run(cuda, f, shape, x, w, b) for f in fams]
+    for f, o in zip(fams[1:], outs[1:]):
+        assert np.array_equal(o, outs[0]), f"{f} != {fams[0]}"
+
+
+def test_linearity_in_bias(cuda):
+    # y(b + d) - y(b) == d broadcast over channels, at full size.
+    shape = m.load_workloads()["cfg5b_dilated_3x3"]
+    x, w, b = m.make_inputs(shape, seed=5)
+    y0 = _run(cuda, "auto", shape, x, w, b).reshape(-1, shape.k)
+    d = np.arange(shape.k, dtype=np.int32) * 7 - 300
+    y1 = _run(cuda, "auto", shape, x, w, b + d).reshape(-1, shape.k)
+    assert np.array_equal(y1 - y0, np.broadcast_to(d, y0.shape))
+
+
+REFERENCE_WORKLOADS = [name for name, _ in m.shape.iter_reference_workloads()]
+
+
+@pytest.mark.parametrize("name", REFERENCE_WORKLOADS)
+def test_reference_workloads(cuda, name):
+    shape = m.load_workloads()[name]
+    x, w, b = m.make_inputs(shape, values="full")
+    small = _reduced(shape, 2e9)
+    for fam in _families(shape):
+        if small is shape:
+            got = _run(cuda, fam, shape, x, w, b)
+            assert np.array_equal(got, pyoracle.conv(shape, x, w, b)), fam
+        else:
+            got = _run(cuda, fam, shape, x, w, b)
+            _sampled_check(shape, x, w, b, got, samples=50_000, whole_images=(0,))
+
+
+def _random_shapes(count, seed=2026):
+    rng = np.random.RandomState(seed)
+    out = []
+    while len(out) < count:
+        r, s = rng.randint(1, 6), rng.randint(1, 6)
+        sh = m.ConvShape(
+            n=int(rng.randint(1, 4)), h=int(rng.randint(1, 24)), w=int(rng.randint(1, 24)),
+            c=int(16 * rng.randint(1, 12)), k=int(rng.randint(1, 300)), r=int(r), s=int(s),
+            pad_h=int(rng.randint(0, 3)), pad_w=int(rng.randint(0, 3)),
+            stride_h=int(rng.randint(1, 4)), stride_w=int(rng.randint(1, 4)),
+            dilation_h=int(rng.randint(1, 3)), dilation_w=int(rng.randint(1, 3)))
+        if sh.valid and sh.eligible("generic"):
+            out.append(sh)
+    return out
+
+
+@pytest.mark.parametrize("idx,shape", list(enumerate(_random_shapes(40))))
+def test_random_shapes(cuda, idx, shape):
+    x, w, b = m.make_inputs(shape, seed=idx)
+    want = pyoracle.conv(shape, x, w, b)
+    for fam in _families(shape):
+        got = _run(cuda, fam, shape, x, w, b)
+        assert np.array_equal(got, want), f"{fam} on {shape}"
+
+
+def test_reference_value_range(cuda):
+    # The reference's own value distribution ([-4,4], bias [-31,31]).
+    shape = m.load_workloads()["resnet_s3_3x3"]
+    x, w, b = m.make_inputs(shape, values="reference")
+    got = _run(cuda, "auto", shape, x, w, b)
+    assert np.array_equal(got, pyoracle.conv(shape, x, w, b))
+
+
+def test_stream_argument_and_async(cuda):
+    torch = cuda
+    shape = m.load_workloads()["cfg2_mid_3x3"]
+    x, w, b = m.make_inputs(shape)
+    dx, dw, db = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    dy = torch.zeros(shape.output_elements, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        m.launch_generic(shape, dx, dw, db, dy, stream=s)
+    s.synchronize()
+    assert np.array_equal(dy.cpu().numpy(), pyoracle.conv(shape, x, w, b))
+
+
+def test_ineligible_and_bad_pointer_statuses(cuda):
+    torch = cuda
+    shape = m.load_workloads()["cfg3a_down_3x3_s2"]  # stride 2: strip-ineligible
+    assert not shape.eligible("strip")
+    x = torch.zeros(shape.input_elements, dtype=torch.int8, device="cuda")
+    w = torch.zeros(shape.filter_elements, dtype=torch.int8, device="cuda")
+    b = torch.zeros(shape.k, dtype=torch.int32, device="cuda")
+    y = torch.zeros(shape.output_elements, dtype=torch.int32, device="cuda")
+    with pytest.raises(m.Int8ConvError) as err:
+        m.launch_spatial_strip(shape, x, w, b, y)
+    assert err.value.status == _abi.NOT_ELIGIBLE
+    st = _abi.lib.int8conv_launch_generic(shape.c_struct(), x.data_ptr() + 1, w.data_ptr(),
+                                          b.data_ptr(), y.data_ptr(), None)
+    assert st == _abi.BAD_POINTER
+
+
+def test_device_wait_timeout_is_reported_and_context_survives(cuda):
+    # Failure detection without a GPU fault: the producer is told to issue no
+    # copies, every consumer wait runs out after 20 ms, the kernel unwinds
+    # (TMEM released, nothing in flight) and the host reads DEVICE_TIMEOUT.
+    torch = cuda
+    shape = m.load_workloads()["cfg1_smoke"]
+    x, w, b = m.make_inputs(shape)
+    dx, dw, db = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    dy = torch.zeros(shape.output_elements, dtype=torch.int32, device="cuda")
+    m.set_wait_limit_ns(20_000_000)
+    m.debug_starve_producer(True)
+    try:
+        m.launch("generic", shape, dx, dw, db, dy)
+        assert m.device_status() == _abi.DEVICE_TIMEOUT
+    finally:
+        m.debug_starve_producer(False)
+        m.set_wait_limit_ns(0)
+    assert m.device_status() == _abi.OK  # flag cleared
+    m.launch("generic", shape, dx, dw, db, dy)
+    assert m.device_status() == _abi.OK
+    assert np.array_equal(dy.cpu().numpy(), pyoracle.conv(shape, x, w, b))

@@ -1,0 +1,50 @@
+"""Eligibility predicates and the workloads table (host only)."""
+import pytest
+
+import int8_kernel_lab_b200 as m
+
+
+def reference_strip_predicate(s):
+    # include/spatial_strip.cuh:11-15 of the reference.
+    return (s.r == 3 and s.s == 3 and s.stride_w == 1 and s.dilation_w == 1 and s.c % 64 == 0
+            and s.k % 64 == 0 and s.out_w % 128 == 0)
+
+
+def test_workloads_table_has_reference_rows_and_baseline():
+    table = m.load_workloads()
+    ref = dict(m.shape.iter_reference_workloads())
+    assert len(ref) == 41
+    for name in m.BASELINE_CASES:
+        assert name in table
+    assert table["big_3x3_s1"] == m.ConvShape(16, 256, 256, 256, 256, 3, 3, 1, 1, 1, 1, 1, 1)
+
+
+def test_every_workload_is_generic_eligible():
+    for name, s in m.load_workloads().items():
+        assert s.valid and s.eligible("generic"), name
+
+
+def test_reference_strip_shapes_stay_strip_eligible():
+    # Drop-in property: whatever the reference could run as strip, the B200
+    # strip family accepts too (only big_3x3_s1 in the table).
+    ref_strip = [n for n, s in m.load_workloads().items() if reference_strip_predicate(s)]
+    assert ref_strip == ["big_3x3_s1"]
+    for name in ref_strip:
+        assert m.load_workloads()[name].eligible("strip")
+
+
+@pytest.mark.parametrize("name,expect", [
+    ("cfg2_mid_3x3", True), ("cfg5a_stress_3x3", True), ("cfg5c_1x7", True),
+    ("cfg5b_dilated_3x3", False),   # dilation_w 2
+    ("cfg3a_down_3x3_s2", False),   # stride_w 2
+    ("cfg3b_pointwise", False),     # s == 1: nothing to reuse
+])
+def test_strip_predicate(name, expect):
+    assert m.load_workloads()[name].eligible("strip") is expect
+
+
+def test_ops_and_bytes_accounting():
+    s = m.load_workloads()["cfg5a_stress_3x3"]
+    assert s.ops == 2 * 256 * 56 * 56 * 256 * 256 * 9
+    assert s.compulsory_bytes == (256 * 56 * 56 * 256 + 256 * 9 * 256 + 4 * 256
+                                  + 4 * 256 * 56 * 56 * 256)
