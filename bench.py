@@ -131,11 +131,9 @@ class ClockSampler:
 
 
 def shard(n: int, rank: int, world: int):
-    """Images [start, stop) of `rank`: an even split of the batch."""
-    per = n // world
-    extra = n % world
-    start = rank * per + min(rank, extra)
-    return start, start + per + (1 if rank < extra else 0)
+    """Images [start, stop) of `rank` (int8_kernel_lab_b200.sharding)."""
+    from int8_kernel_lab_b200.sharding import shard_range
+    return shard_range(n, rank, world)
 
 
 # ---------------------------------------------------------------------------
@@ -426,21 +424,15 @@ def verify_sharded(full, dxs, dys, dw, db, local_shape, x, strategy, dist, rank,
     import torch
 
     import int8_kernel_lab_b200 as m
-    counts = [shard(full.n, r, world) for r in range(world)]
-    per_img = full.out_h * full.out_w * full.k
-    parts = [torch.empty((c1 - c0) * per_img, dtype=torch.int32, device="cuda")
-             for c0, c1 in counts]
-    mine = dys[0]
-    if rank == 0:
-        dist.gather(mine, gather_list=parts, dst=0)
-        gathered = torch.cat(parts)
-        xall = torch.from_numpy(x).cuda()
-        yall = torch.empty(full.output_elements, dtype=torch.int32, device="cuda")
-        m.launch(strategy if full.eligible(strategy) else "generic", full, xall, dw, db, yall)
-        torch.cuda.synchronize()
-        return bool(torch.equal(gathered, yall))
-    dist.gather(mine, dst=0)
-    return None
+    from int8_kernel_lab_b200.sharding import gather_outputs
+    gathered = gather_outputs(dys[0], full, rank, world, dist)
+    if rank != 0:
+        return None
+    xall = torch.from_numpy(x).cuda()
+    yall = torch.empty(full.output_elements, dtype=torch.int32, device="cuda")
+    m.launch(strategy if full.eligible(strategy) else "generic", full, xall, dw, db, yall)
+    torch.cuda.synchronize()
+    return bool(torch.equal(gathered, yall))
 
 
 def main():

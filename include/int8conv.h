@@ -151,6 +151,13 @@ void int8conv_set_wait_limit_ns(uint64_t ns);
  * flight and the context stays usable. */
 void int8conv_debug_starve_producer(int on);
 
+/* CTA pairing of the GENERIC and STRIP kernels (process-wide):
+ * 0 = automatic (pairs of CTAs sharing one 256-row tensor-core tile through
+ * tcgen05 cta_group::2 when the problem has enough tiles to fill the GPU),
+ * 1 = single CTAs only, 2 = pairs whenever the shape allows.  Every mode
+ * computes identical results; the choice only moves performance. */
+int8conv_status int8conv_set_cta_pairing(int mode);
+
 /* Number of kernels this library has launched in this process. */
 uint64_t int8conv_launch_count(void);
 

@@ -121,5 +121,13 @@ def set_wait_limit_ns(ns: int) -> None:
     _abi.lib.int8conv_set_wait_limit_ns(int(ns))
 
 
+PAIRING = {"auto": 0, "single": 1, "pair": 2}
+
+
+def set_cta_pairing(mode: str) -> None:
+    """'auto' | 'single' | 'pair': how the GENERIC/STRIP kernels group CTAs."""
+    _abi.check(_abi.lib.int8conv_set_cta_pairing(PAIRING[mode]), "set_cta_pairing")
+
+
 def debug_starve_producer(on: bool) -> None:
     _abi.lib.int8conv_debug_starve_producer(1 if on else 0)

@@ -12,6 +12,7 @@ namespace i8c {
 extern std::atomic<uint64_t> g_wait_limit_ns;
 extern std::atomic<uint32_t> g_starve;
 extern std::atomic<uint64_t> g_launches;
+extern std::atomic<int> g_pairing;
 }  // namespace i8c
 
 namespace {
@@ -185,5 +186,11 @@ void int8conv_set_wait_limit_ns(uint64_t ns) {
 void int8conv_debug_starve_producer(int on) { i8c::g_starve.store(on ? 1u : 0u); }
 
 uint64_t int8conv_launch_count(void) { return i8c::g_launches.load(); }
+
+int8conv_status int8conv_set_cta_pairing(int mode) {
+  if (mode < 0 || mode > 2) return INT8CONV_BAD_ARGUMENT;
+  i8c::g_pairing.store(mode);
+  return INT8CONV_OK;
+}
 
 }  // extern "C"

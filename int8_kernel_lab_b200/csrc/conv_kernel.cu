@@ -7,22 +7,32 @@
 //   out[m*K + k] = bias[k] + sum_{r,s,c} X[n, oy*sh + r*dh - ph, ox*sw + s*dw - pw, c] * W[k,r,s,c]
 // with padding taps contributing nothing (here: zero-filled by TMA).
 //
-// B200 design (one persistent CTA per SM, 6 warps):
+// B200 design (persistent CTAs, 6 warps each):
 //   warp 0     TMA producer.  Activations come through an im2col tensor map
 //              (padding, stride and dilation are done by the TMA unit:
 //              bounding-box corners, traversal strides, per-tap offsets),
 //              filters through a tiled map over W viewed as [K][R*S][C].
 //              Tiles land swizzled (SW128/64/32 for 128/64/32-byte channel
 //              blocks) in mbarrier-guarded rings.
-//   warp 1     MMA issuer: tcgen05.mma.cta_group::1.kind::i8, M=128, N=BN,
-//              K=32 bytes per instruction, int32 accumulators in TMEM.  Two
-//              accumulator buffers let the epilogue of tile i overlap the
-//              mainloop of tile i+1.
-//   warps 2-5  epilogue: tcgen05.ld (one output pixel per thread), + bias,
-//              16-byte int32 stores of the NHWK output.
+//   warp 1     MMA issuer: tcgen05.mma kind::i8, K=32 bytes per instruction,
+//              int32 accumulators in TMEM.  Two accumulator buffers let the
+//              epilogue of tile i overlap the mainloop of tile i+1.
+//   warps 2-5  epilogue: tcgen05.ld (one output pixel row per thread), a
+//              transpose through swizzled shared memory, + bias, and streaming
+//              16-byte stores in which each warp instruction writes whole
+//              128-byte segments of four NHWK output rows.
 //
-// GENERIC: per k-block (tap r,s x channel block) one A tile of 128 output
-//   pixels and one B tile.
+// Single CTA (PAIR = false): cta_group::1, M = 128 rows per tile.
+// CTA pair (PAIR = true, cluster of 2): cta_group::2, M = 256 rows per tile.
+//   Each CTA loads its own 128 rows of A and half of the BN filter rows of B;
+//   the leader (rank 0) arms its barriers for both CTAs' bytes and issues the
+//   MMAs, which read A and B from both CTAs' shared memory, so every filter
+//   tile crosses L2 -> SM once per 256 output rows instead of once per 128.
+//   Commits arrive on both CTAs' barriers; each epilogue drains its own TMEM
+//   and releases the accumulator on the leader.
+//
+// GENERIC: per k-block (tap r,s x channel block) one A tile of output pixels
+//   and one B tile.
 // STRIP (stride_w = dilation_w = 1): the M dimension runs over padded-row
 //   positions (n, oy, j), j < Wp = out_w + S - 1.  Per (r, channel block) ONE
 //   im2col load of 128 + S - 1 consecutive positions feeds all S filter
@@ -58,21 +68,25 @@ struct SwizzleOf<32> {
   static constexpr Layout kLayout = Layout::kSw32;
 };
 
+constexpr uint32_t kEpilogueStaging = 4 * 32 * 128;
+constexpr uint32_t kOneCtaPerSm = kMaxSmem / 2 + 1024;
+
 // Shared-memory plan, identical on host and device.
 struct SmemPlan {
-  uint32_t a_bytes, b_bytes;  // one stage of A / B
-  uint32_t a_off, b_off, bar_off;
+  uint32_t a_bytes, b_bytes;  // one stage of A / B (this CTA's share)
+  uint32_t a_off, b_off, stage_off, bar_off;
   uint32_t total;             // bytes requested at launch (incl. alignment slack)
 };
 
-__host__ __device__ inline SmemPlan smem_plan(int cblk, int bn, int a_rows, int a_stages,
+__host__ __device__ inline SmemPlan smem_plan(int cblk, int b_rows, int a_rows, int a_stages,
                                               int b_stages) {
   SmemPlan p;
   p.a_bytes = a_rows * cblk;
-  p.b_bytes = bn * cblk;
+  p.b_bytes = b_rows * cblk;
   p.a_off = 0;
   p.b_off = p.a_off + a_stages * p.a_bytes;
-  p.bar_off = p.b_off + b_stages * p.b_bytes;
+  p.stage_off = p.b_off + b_stages * p.b_bytes;  // epilogue staging, 4 warps x 32 x 128 B
+  p.bar_off = p.stage_off + kEpilogueStaging;
   // a_full/a_empty[a_stages], b_full/b_empty[b_stages], tfull[2], tempty[2], drain, slot
   const uint32_t bar_bytes = (2 * a_stages + 2 * b_stages + 5) * 8 + 8;
   p.total = 1024 + p.bar_off + bar_bytes;
@@ -97,20 +111,32 @@ struct Ring {
   }
 };
 
-template <int CBLK, bool STRIP>
+template <bool PAIR>
+__device__ __forceinline__ void commit_to(uint64_t *bar) {
+  if constexpr (PAIR)
+    umma_commit_pair(bar, 0x3);
+  else
+    umma_commit(bar);
+}
+
+template <int CBLK, bool STRIP, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_w, const ConvGeom g,
                 const int32_t *__restrict__ bias, int32_t *__restrict__ out, const RunCtl ctl) {
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte alignment: the SW128 atom (8 rows x 128 B) starts on it.
+  // 1024-byte alignment: the SW128 atom (8 rows x 128 B) starts on it.  The
+  // offset is the same in both CTAs of a pair (same kernel, same smem size).
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  constexpr int kTileRows = PAIR ? 2 * kBlockM : kBlockM;
   const int a_stages = STRIP ? g.a_stages : g.stages;
   const int a_rows = STRIP ? g.a_rows : kBlockM;
-  const SmemPlan plan = smem_plan(CBLK, g.bn, a_rows, a_stages, g.stages);
+  const int b_rows = PAIR ? g.bn / 2 : g.bn;
+  const SmemPlan plan = smem_plan(CBLK, b_rows, a_rows, a_stages, g.stages);
   uint8_t *a_ring = smem + plan.a_off;
   uint8_t *b_ring = smem + plan.b_off;
+  int4 *staging = reinterpret_cast<int4 *>(smem + plan.stage_off);
   uint64_t *a_full = reinterpret_cast<uint64_t *>(smem + plan.bar_off);
   uint64_t *a_empty = a_full + a_stages;
   uint64_t *b_full = a_empty + a_stages;
@@ -125,6 +151,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const WaitCtx wctx{ctl.wait_ns, ctl.status};
   const int m_span = STRIP ? g.PWp : g.PQ;     // positions per image
   const int m_row = STRIP ? g.Wp : g.Q;        // positions per output row
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int tile_first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tile_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < a_stages; ++i) {
@@ -137,7 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4 * 32);
+      // One arrival per epilogue warp (of both CTAs for a pair).
+      mbar_init(&tempty[i], PAIR ? 8 : 4);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -145,11 +176,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_w);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, g.tmem_cols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, g.tmem_cols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, g.tmem_cols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // A pair signals each other's barriers: both must be initialised first.
+  if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -157,15 +195,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       Ring ra, rb;
-      long issued_a = 0, issued_b = 0;
+      long armed_a = 0, armed_b = 0;
       const uint32_t a_tx = (STRIP ? g.strip_px : kBlockM) * CBLK;
       const uint32_t b_tx = plan.b_bytes;
+      // A pair credits all bytes to the leader's barriers, armed for both CTAs.
+      const uint32_t tx_mult = PAIR ? 2u : 1u;
+      auto full_addr = [&](uint64_t *bar) -> uint32_t {
+        return PAIR ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar);
+      };
       bool ok = true;
-      for (int tile = blockIdx.x; tile < g.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = tile_first; tile < g.num_tiles && ok; tile += tile_step) {
         const int m_tile = tile / g.n_tiles;
         const int n_tile = tile - m_tile * g.n_tiles;
-        const int m0 = m_tile * kBlockM;
-        const int n0 = n_tile * g.bn;
+        const int m0 = m_tile * kTileRows + static_cast<int>(rank) * kBlockM;
+        const int n0 = n_tile * g.bn + static_cast<int>(rank) * b_rows;
         const int img = m0 / m_span;
         const int rem = m0 - img * m_span;
         const int p = rem / m_row;
@@ -180,11 +223,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               if (!ctl.starve) {
-                mbar_arrive_expect_tx(&a_full[ra.stage], a_tx);
-                tma_load_im2col_4d(a_ring + ra.stage * plan.a_bytes, &tmap_x, &a_full[ra.stage],
-                                   cb * CBLK, x_w, x_h, img, 0,
-                                   static_cast<uint16_t>(r * g.dil_h));
-                ++issued_a;
+                if (leader) {
+                  mbar_arrive_expect_tx(&a_full[ra.stage], tx_mult * a_tx);
+                  ++armed_a;
+                }
+                void *dst = a_ring + ra.stage * plan.a_bytes;
+                const uint16_t oh = static_cast<uint16_t>(r * g.dil_h);
+                if constexpr (PAIR)
+                  tma_load_im2col_4d_pair(dst, &tmap_x, full_addr(&a_full[ra.stage]), cb * CBLK,
+                                          x_w, x_h, img, 0, oh);
+                else
+                  tma_load_im2col_4d(dst, &tmap_x, &a_full[ra.stage], cb * CBLK, x_w, x_h, img,
+                                     0, oh);
               }
               ra.next(a_stages);
               for (int s = 0; s < g.S; ++s) {
@@ -193,10 +243,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                   break;
                 }
                 if (!ctl.starve) {
-                  mbar_arrive_expect_tx(&b_full[rb.stage], b_tx);
-                  tma_load_3d(b_ring + rb.stage * plan.b_bytes, &tmap_w, &b_full[rb.stage],
-                              cb * CBLK, r * g.S + s, n0);
-                  ++issued_b;
+                  if (leader) {
+                    mbar_arrive_expect_tx(&b_full[rb.stage], tx_mult * b_tx);
+                    ++armed_b;
+                  }
+                  void *dst = b_ring + rb.stage * plan.b_bytes;
+                  if constexpr (PAIR)
+                    tma_load_3d_pair(dst, &tmap_w, full_addr(&b_full[rb.stage]), cb * CBLK,
+                                     r * g.S + s, n0);
+                  else
+                    tma_load_3d(dst, &tmap_w, &b_full[rb.stage], cb * CBLK, r * g.S + s, n0);
                 }
                 rb.next(g.stages);
               }
@@ -211,13 +267,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ctl.starve) {
               // A and B of one k-block share a stage index and one barrier.
-              mbar_arrive_expect_tx(&b_full[rb.stage], a_tx + b_tx);
-              tma_load_im2col_4d(a_ring + rb.stage * plan.a_bytes, &tmap_x, &b_full[rb.stage],
-                                 cb * CBLK, x_w, x_h, img, static_cast<uint16_t>(s * g.dil_w),
-                                 static_cast<uint16_t>(r * g.dil_h));
-              tma_load_3d(b_ring + rb.stage * plan.b_bytes, &tmap_w, &b_full[rb.stage], cb * CBLK,
-                          tap, n0);
-              ++issued_b;
+              if (leader) {
+                mbar_arrive_expect_tx(&b_full[rb.stage], tx_mult * (a_tx + b_tx));
+                ++armed_b;
+              }
+              void *adst = a_ring + rb.stage * plan.a_bytes;
+              void *bdst = b_ring + rb.stage * plan.b_bytes;
+              const uint16_t ow = static_cast<uint16_t>(s * g.dil_w);
+              const uint16_t oh = static_cast<uint16_t>(r * g.dil_h);
+              if constexpr (PAIR) {
+                const uint32_t bar = full_addr(&b_full[rb.stage]);
+                tma_load_im2col_4d_pair(adst, &tmap_x, bar, cb * CBLK, x_w, x_h, img, ow, oh);
+                tma_load_3d_pair(bdst, &tmap_w, bar, cb * CBLK, tap, n0);
+              } else {
+                tma_load_im2col_4d(adst, &tmap_x, &b_full[rb.stage], cb * CBLK, x_w, x_h, img,
+                                   ow, oh);
+                tma_load_3d(bdst, &tmap_w, &b_full[rb.stage], cb * CBLK, tap, n0);
+              }
             }
             rb.next(g.stages);
             if (++cb == g.cblocks) {
@@ -232,27 +298,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Copies still in flight must land before the CTA exits: wait for the
-      // fills this thread armed most recently (immediate on the normal path).
-      for (long i = 0, n = issued_b < g.stages ? issued_b : g.stages; i < n; ++i) {
+      // fills armed most recently (immediate on the normal path).  For a pair
+      // the leader's barriers count both CTAs' copies.
+      for (long i = 0, n = armed_b < g.stages ? armed_b : g.stages; i < n; ++i) {
         rb.prev(g.stages);
         mbar_wait(&b_full[rb.stage], rb.phase, wctx, kStatusTimeoutTeardown);
       }
-      for (long i = 0, n = issued_a < a_stages ? issued_a : a_stages; i < n; ++i) {
+      for (long i = 0, n = armed_a < a_stages ? armed_a : a_stages; i < n; ++i) {
         ra.prev(a_stages);
         mbar_wait(&a_full[ra.stage], ra.phase, wctx, kStatusTimeoutTeardown);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      const uint32_t idesc = idesc_s8(kBlockM, g.bn);
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (the leader of a pair) ----------------
+      const uint32_t idesc = idesc_s8(kTileRows, g.bn);
       constexpr Layout kLayout = SwizzleOf<CBLK>::kLayout;
       constexpr uint32_t kAtom = 8 * CBLK;  // 8 rows x CBLK bytes
       Ring ra, rb;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < g.num_tiles && ok; tile += gridDim.x) {
+      auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t accumulate) {
+        if constexpr (PAIR)
+          umma_i8_pair(d, a, b, idesc, accumulate);
+        else
+          umma_i8(d, a, b, idesc, accumulate);
+      };
+      for (int tile = tile_first; tile < g.num_tiles && ok; tile += tile_step) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, wctx, kStatusTimeoutDrain)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * g.acc_stride);
@@ -274,17 +347,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int k = 0; k < CBLK / 32; ++k) {
                 // Filter column s reads the strip s rows further on.
-                const uint64_t a_desc =
-                    smem_desc(a_addr + s * CBLK + 32 * k, 16, kAtom, kLayout);
-                const uint64_t b_desc = smem_desc(b_addr + 32 * k, 16, kAtom, kLayout);
-                umma_i8(d_tmem, a_desc, b_desc, idesc, accumulate);
+                mma(d_tmem, smem_desc(a_addr + s * CBLK + 32 * k, 16, kAtom, kLayout),
+                    smem_desc(b_addr + 32 * k, 16, kAtom, kLayout), accumulate);
                 accumulate = 1;
               }
-              umma_commit(&b_empty[rb.stage]);
+              commit_to<PAIR>(&b_empty[rb.stage]);
               rb.next(g.stages);
             }
             if (!ok) break;
-            umma_commit(&a_empty[ra.stage]);
+            commit_to<PAIR>(&a_empty[ra.stage]);
             ra.next(a_stages);
           }
         } else {
@@ -298,24 +369,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b_addr = smem_u32(b_ring + rb.stage * plan.b_bytes);
 #pragma unroll
             for (int k = 0; k < CBLK / 32; ++k) {
-              const uint64_t a_desc = smem_desc(a_addr + 32 * k, 16, kAtom, kLayout);
-              const uint64_t b_desc = smem_desc(b_addr + 32 * k, 16, kAtom, kLayout);
-              umma_i8(d_tmem, a_desc, b_desc, idesc, accumulate);
+              mma(d_tmem, smem_desc(a_addr + 32 * k, 16, kAtom, kLayout),
+                  smem_desc(b_addr + 32 * k, 16, kAtom, kLayout), accumulate);
               accumulate = 1;
             }
-            umma_commit(&b_empty[rb.stage]);
+            commit_to<PAIR>(&b_empty[rb.stage]);
             rb.next(g.stages);
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        commit_to<PAIR>(&tfull[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
-      // Every MMA issued must finish before TMEM is released.
-      umma_commit(drain);
+      // Every MMA issued must finish before TMEM is released (in both CTAs).
+      commit_to<PAIR>(drain);
+      mbar_wait(drain, 0, wctx, kStatusTimeoutTeardown);
+    } else if (lane == 0 && PAIR) {
+      // The peer's TMEM and shared memory stay in use until the leader's MMAs
+      // are done; the leader's final commit arrives here too.
       mbar_wait(drain, 0, wctx, kStatusTimeoutTeardown);
     }
   } else {
@@ -324,12 +398,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     const bool vec_k = (g.K & 3) == 0;
     const int m_limit = STRIP ? g.Mp : g.M;
+    const uint32_t tempty_leader0 =
+        PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
+    const uint32_t tempty_leader1 =
+        PAIR ? mapa_shared(smem_u32(&tempty[1]), 0) : smem_u32(&tempty[1]);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < g.num_tiles; tile += gridDim.x) {
+    for (int tile = tile_first; tile < g.num_tiles; tile += tile_step) {
       const int m_tile = tile / g.n_tiles;
       const int n_tile = tile - m_tile * g.n_tiles;
-      const int pos = m_tile * kBlockM + row;
+      const int pos = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + row;
       const int n0 = n_tile * g.bn;
       bool valid = pos < m_limit;
       int m = pos;
@@ -348,37 +426,64 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * g.acc_stride;
-      int32_t *dst_row = out + static_cast<int64_t>(m) * g.K + n0;
+      // Each 32x32 int32 block (this warp's 32 rows x 32 columns) goes through
+      // swizzled shared memory so the global stores are whole 128-byte row
+      // segments: thread-per-row stores would issue one L2 request per 16 B.
+      int4 *stg = staging + (warp - 2) * 32 * 8;
+      const int q = lane & 7;    // 16-byte column group this lane stores
+      const int rsub = lane >> 3;
       for (int c0 = 0; c0 < g.bn; c0 += 32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + c0, v);
         tmem_ld_wait();
-        if (valid) {
-          const int col0 = n0 + c0;
-          if (vec_k && c0 + 32 <= g.bn && col0 + 32 <= g.K) {
-            const int4 *b4 = reinterpret_cast<const int4 *>(bias + col0);
-            int4 *d4 = reinterpret_cast<int4 *>(dst_row + c0);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int4 bb = __ldg(b4 + j);
-              int4 o;
-              o.x = static_cast<int32_t>(v[4 * j + 0]) + bb.x;
-              o.y = static_cast<int32_t>(v[4 * j + 1]) + bb.y;
-              o.z = static_cast<int32_t>(v[4 * j + 2]) + bb.z;
-              o.w = static_cast<int32_t>(v[4 * j + 3]) + bb.w;
-              d4[j] = o;
-            }
-          } else {
+        for (int j = 0; j < 8; ++j)
+          stg[lane * 8 + (j ^ (lane & 7))] =
+              make_int4(static_cast<int32_t>(v[4 * j]), static_cast<int32_t>(v[4 * j + 1]),
+                        static_cast<int32_t>(v[4 * j + 2]), static_cast<int32_t>(v[4 * j + 3]));
+        __syncwarp();
+        const int col0 = n0 + c0;
+        if (vec_k) {
+          // K % 4 == 0: 16-byte groups are wholly inside or outside [0, K).
+          const bool col_ok = c0 + 4 * q < g.bn && col0 + 4 * q < g.K;
+          const int4 bb = col_ok ? __ldg(reinterpret_cast<const int4 *>(bias + col0) + q)
+                                 : make_int4(0, 0, 0, 0);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (c0 + j < g.bn && col0 + j < g.K)
-                dst_row[c0 + j] = static_cast<int32_t>(v[j]) + __ldg(bias + col0 + j);
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + rsub;
+            const int mr = __shfl_sync(0xffffffffu, m, r);
+            const bool vr = __shfl_sync(0xffffffffu, valid ? 1 : 0, r) != 0;
+            if (vr && col_ok) {
+              int4 o = stg[r * 8 + (q ^ (r & 7))];
+              o.x += bb.x;
+              o.y += bb.y;
+              o.z += bb.z;
+              o.w += bb.w;
+              __stcs(reinterpret_cast<int4 *>(out + static_cast<int64_t>(mr) * g.K + col0) + q, o);
             }
           }
+        } else {
+          const bool col_ok = c0 + lane < g.bn && col0 + lane < g.K;
+          const int32_t bl = col_ok ? __ldg(bias + col0 + lane) : 0;
+          const int32_t *stg32 = reinterpret_cast<const int32_t *>(stg);
+          for (int r = 0; r < 32; ++r) {
+            const int mr = __shfl_sync(0xffffffffu, m, r);
+            const bool vr = __shfl_sync(0xffffffffu, valid ? 1 : 0, r) != 0;
+            if (vr && col_ok)
+              out[static_cast<int64_t>(mr) * g.K + col0 + lane] =
+                  stg32[(r * 8 + ((lane >> 2) ^ (r & 7))) * 4 + (lane & 3)] + bl;
+          }
         }
+        __syncwarp();
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+        else
+          mbar_arrive(&tempty[acc]);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -388,10 +493,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // Neither CTA of a pair leaves while the other may still touch its shared
+  // memory (remote barrier arrivals, MMA operand reads).
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, g.tmem_cols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, g.tmem_cols);
+    else
+      tmem_dealloc(tmem_base, g.tmem_cols);
   }
 }
 
@@ -420,7 +531,8 @@ static int next_pow2(int v) {
 }
 
 // Fills the launch geometry; false if the shape does not fit the kernel.
-static bool plan_geometry(const int8conv_shape &s, bool strip, ConvGeom &g, int &cblk) {
+static bool plan_geometry(const int8conv_shape &s, bool strip, bool pair, ConvGeom &g,
+                          int &cblk) {
   const int32_t out_h = (s.h + 2 * s.pad_h - s.dilation_h * (s.r - 1) - 1) / s.stride_h + 1;
   const int32_t out_w = (s.w + 2 * s.pad_w - s.dilation_w * (s.s - 1) - 1) / s.stride_w + 1;
   cblk = pick_cblk(s.c);
@@ -441,48 +553,50 @@ static bool plan_geometry(const int8conv_shape &s, bool strip, ConvGeom &g, int 
   g.cblocks = (s.c + cblk - 1) / cblk;
   g.kblocks = s.r * s.s * g.cblocks;
   g.bn = pick_bn(s.k);
+  g.pair = pair ? 1 : 0;
   g.acc_stride = (g.bn + 31) / 32 * 32;
   g.tmem_cols = next_pow2(2 * g.acc_stride);
   if (g.tmem_cols > 512) return false;
-  const int b_bytes = g.bn * cblk;
-  const int budget = kMaxSmem - 1024 - 512;
+  const int tile_rows = pair ? 2 * kBlockM : kBlockM;
+  const int b_bytes = (pair ? g.bn / 2 : g.bn) * cblk;
+  const int budget = kMaxSmem - 1024 - 512 - static_cast<int>(kEpilogueStaging);
+  int64_t positions = g.M;
   if (strip) {
     g.Wp = out_w + s.s - 1;
     g.PWp = out_h * g.Wp;
-    const int64_t mp = static_cast<int64_t>(s.n) * g.PWp;
-    if (mp >= (int64_t(1) << 31)) return false;
-    g.Mp = static_cast<int32_t>(mp);
+    positions = static_cast<int64_t>(s.n) * g.PWp;
+    if (positions >= (int64_t(1) << 31)) return false;
+    g.Mp = static_cast<int32_t>(positions);
     g.strip_px = kBlockM + s.s - 1;
     g.a_rows = (g.strip_px + 7) / 8 * 8;
     const int a_bytes = g.a_rows * cblk;
     // Strip ring: enough strips to keep S filter tiles per strip flowing.
     g.a_stages = 3;
     int b_stages = (budget - g.a_stages * a_bytes) / b_bytes;
-    if (b_stages > 8) b_stages = 8;
+    if (b_stages > 12) b_stages = 12;
     if (b_stages < 2) {
       g.a_stages = 2;
       b_stages = (budget - g.a_stages * a_bytes) / b_bytes;
-      if (b_stages > 8) b_stages = 8;
+      if (b_stages > 12) b_stages = 12;
     }
     if (b_stages < 2) return false;
     g.stages = b_stages;
-    g.m_tiles = (g.Mp + kBlockM - 1) / kBlockM;
   } else {
     const int per_stage = kBlockM * cblk + b_bytes;
     int stages = budget / per_stage;
-    if (stages > 8) stages = 8;
+    if (stages > 12) stages = 12;
     if (stages < 2) return false;
     g.stages = stages;
     g.a_stages = stages;
     g.a_rows = kBlockM;
-    g.m_tiles = (g.M + kBlockM - 1) / kBlockM;
   }
+  g.m_tiles = static_cast<int32_t>((positions + tile_rows - 1) / tile_rows);
   g.n_tiles = (s.k + g.bn - 1) / g.bn;
   g.num_tiles = g.m_tiles * g.n_tiles;
   return true;
 }
 
-template <int CBLK, bool STRIP>
+template <int CBLK, bool STRIP, bool PAIR>
 static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, const int8_t *x,
                                 const int8_t *w, const int32_t *b, int32_t *y,
                                 cudaStream_t stream) {
@@ -490,19 +604,67 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   CUtensorMap maps[2];
   const int pixels = STRIP ? g.strip_px : kBlockM;
   const int count_w = STRIP ? g.Wp : g.Q;
+  const int b_rows = PAIR ? g.bn / 2 : g.bn;
   int8conv_status st = activation_map_im2col(s, x, CBLK, pixels, count_w, &maps[0]);
   if (st != INT8CONV_OK) return st;
-  st = filter_map_tiled(s, w, CBLK, g.bn, &maps[1]);
+  st = filter_map_tiled(s, w, CBLK, b_rows, &maps[1]);
   if (st != INT8CONV_OK) return st;
-  const SmemPlan plan =
-      smem_plan(CBLK, g.bn, STRIP ? g.a_rows : kBlockM, g.a_stages, g.stages);
-  auto kernel = conv_kernel<CBLK, STRIP>;
-  if (!ensure_smem_attr(reinterpret_cast<const void *>(kernel), plan.total))
+  const SmemPlan plan = smem_plan(CBLK, b_rows, STRIP ? g.a_rows : kBlockM, g.a_stages, g.stages);
+  auto kernel = conv_kernel<CBLK, STRIP, PAIR>;
+  // At least half an SM's shared memory: one CTA per SM, so a CTA never waits
+  // for another's TMEM columns.
+  const uint32_t smem_bytes = plan.total > kOneCtaPerSm ? plan.total : kOneCtaPerSm;
+  if (!ensure_smem_attr(reinterpret_cast<const void *>(kernel), smem_bytes))
     return INT8CONV_CUDA_ERROR;
-  const int grid = g.num_tiles < dev.sm_count ? g.num_tiles : dev.sm_count;
-  kernel<<<grid, kThreads, plan.total, stream>>>(maps[0], maps[1], g, b, y, run_ctl());
+  const RunCtl ctl = run_ctl();
+  cudaError_t err;
+  if constexpr (PAIR) {
+    const int pairs = g.num_tiles < dev.sm_count / 2 ? g.num_tiles : dev.sm_count / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], g, b, y, ctl);
+  } else {
+    const int grid = g.num_tiles < dev.sm_count ? g.num_tiles : dev.sm_count;
+    kernel<<<grid, kThreads, smem_bytes, stream>>>(maps[0], maps[1], g, b, y, ctl);
+    err = cudaGetLastError();
+  }
   note_launch();
-  return cudaGetLastError() == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
+  return err == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
+}
+
+template <bool STRIP, bool PAIR>
+static int8conv_status launch_cblk(const int8conv_shape &s, const ConvGeom &g, int cblk,
+                                   const int8_t *x, const int8_t *w, const int32_t *b,
+                                   int32_t *y, cudaStream_t stream) {
+  switch (cblk) {
+    case 128:
+      return launch_t<128, STRIP, PAIR>(s, g, x, w, b, y, stream);
+    case 64:
+      return launch_t<64, STRIP, PAIR>(s, g, x, w, b, y, stream);
+    default:
+      return launch_t<32, STRIP, PAIR>(s, g, x, w, b, y, stream);
+  }
+}
+
+// CTA pairs pay off once there are enough 256-row tiles to fill every SM.
+static bool use_pair(const int8conv_shape &s, bool strip) {
+  const int mode = pairing_mode();
+  if (mode == 1) return false;
+  ConvGeom g;
+  int cblk = 0;
+  if (!plan_geometry(s, strip, true, g, cblk)) return false;
+  if (mode == 2) return true;
+  return g.num_tiles >= device_info().sm_count / 2;
 }
 
 template <bool STRIP>
@@ -510,15 +672,12 @@ static int8conv_status launch_family(const int8conv_shape &s, const int8_t *x, c
                                      const int32_t *b, int32_t *y, cudaStream_t stream) {
   ConvGeom g;
   int cblk = 0;
-  if (!plan_geometry(s, STRIP, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
-  switch (cblk) {
-    case 128:
-      return launch_t<128, STRIP>(s, g, x, w, b, y, stream);
-    case 64:
-      return launch_t<64, STRIP>(s, g, x, w, b, y, stream);
-    default:
-      return launch_t<32, STRIP>(s, g, x, w, b, y, stream);
+  if (use_pair(s, STRIP)) {
+    if (!plan_geometry(s, STRIP, true, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+    return launch_cblk<STRIP, true>(s, g, cblk, x, w, b, y, stream);
   }
+  if (!plan_geometry(s, STRIP, false, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+  return launch_cblk<STRIP, false>(s, g, cblk, x, w, b, y, stream);
 }
 
 int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,

@@ -4,7 +4,7 @@
 //   * same flags: --strategy, --csv, --warmup N (20), --iterations N (101)
 //     (conv_lab.cu:112-145), plus --case/--config to pick a workloads.csv row
 //     at run time (the reference compiles one binary per case), --values,
-//     --seed, --batch, --peak-tops, --no-graph;
+//     --seed, --batch, --peak-tops, --no-graph, --pairing;
 //   * same flow: seeded inputs, device buffers, launch, validate before
 //     timing, per-launch event median (conv_lab.cu:88-110), winner, CSV or
 //     human line, exit code 0 only if every run was correct and one ran
@@ -72,13 +72,14 @@ struct Options {
   int batch = 0;
   double peak_tops = 4500.0;
   bool graph = true;
+  int pairing = 0;
 };
 
 [[noreturn]] void usage() {
   std::cerr << "usage: conv_lab [--strategy generic|strip|halo|splitk|both|all|auto] [--csv] "
                "[--warmup N] [--iterations N] [--case NAME] [--config CSV] "
                "[--values full|reference] [--seed S] [--batch N] [--peak-tops T] "
-               "[--no-graph]\n";
+               "[--no-graph] [--pairing auto|single|pair]\n";
   std::exit(EXIT_FAILURE);
 }
 
@@ -101,7 +102,11 @@ Options parse_options(int argc, char **argv) {
     else if (arg == "--seed") o.seed = static_cast<uint32_t>(std::stoul(value()));
     else if (arg == "--batch") o.batch = std::stoi(value());
     else if (arg == "--peak-tops") o.peak_tops = std::stod(value());
-    else usage();
+    else if (arg == "--pairing") {
+      const std::string v = value();
+      o.pairing = v == "auto" ? 0 : v == "single" ? 1 : v == "pair" ? 2 : -1;
+      if (o.pairing < 0) usage();
+    } else usage();
   }
   const std::vector<std::string> ok = {"generic", "strip", "halo", "splitk", "both", "all", "auto"};
   if (std::find(ok.begin(), ok.end(), o.strategy) == ok.end() || o.warmup < 0 ||
@@ -258,6 +263,7 @@ std::string fmt(double v) {
 
 int main(int argc, char **argv) {
   const Options options = parse_options(argc, argv);
+  int8conv_set_cta_pairing(options.pairing);
   const std::string config = options.config.empty() ? default_config(argv[0]) : options.config;
   int8conv_shape shape;
   if (!load_case(config, options.case_name, shape)) {

@@ -19,6 +19,7 @@ __device__ uint32_t g_device_status;
 std::atomic<uint64_t> g_wait_limit_ns{2000000000ull};
 std::atomic<uint32_t> g_starve{0};
 std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_pairing{0};
 
 namespace {
 
@@ -152,6 +153,8 @@ RunCtl run_ctl() {
 }
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int pairing_mode() { return g_pairing.load(std::memory_order_relaxed); }
 
 bool ensure_smem_attr(const void *kernel, int bytes) {
   // Remember the largest limit already set per (device, kernel).

@@ -30,6 +30,9 @@ RunCtl run_ctl();
 
 void note_launch();
 
+// CTA pairing policy: 0 auto, 1 single CTAs only, 2 pairs whenever possible.
+int pairing_mode();
+
 // Sets the dynamic shared-memory limit of `kernel` once per device.
 bool ensure_smem_attr(const void *kernel, int bytes);
 

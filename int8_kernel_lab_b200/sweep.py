@@ -30,6 +30,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--strategy", default="all")
     ap.add_argument("--values", default="full", choices=("full", "reference"))
+    ap.add_argument("--pairing", default="auto", choices=("auto", "single", "pair"))
     ap.add_argument("--conv-lab", default=str(PKG / "lib" / "conv_lab"))
     args = ap.parse_args(argv)
     with open(args.configs, newline="") as stream:
@@ -45,7 +46,8 @@ def main(argv=None) -> int:
         result = subprocess.run(
             [args.conv_lab, "--case", case, "--config", str(args.configs), "--strategy",
              args.strategy, "--iterations", str(args.iterations), "--warmup", str(args.warmup),
-             "--values", args.values, "--csv"], text=True, capture_output=True)
+             "--values", args.values, "--pairing", args.pairing, "--csv"],
+            text=True, capture_output=True)
         if result.returncode != 0:
             status = 1
             sys.stderr.write(result.stderr)

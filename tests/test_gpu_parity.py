@@ -35,8 +35,17 @@ def _families(shape):
     return [f for f in FAMILIES if shape.eligible(f)]
 
 
+@pytest.fixture(params=["single", "pair"])
+def pairing(request):
+    # GENERIC and STRIP run as single CTAs (cta_group::1) or CTA pairs
+    # (cta_group::2); both must give the oracle's integers.
+    m.set_cta_pairing(request.param)
+    yield request.param
+    m.set_cta_pairing("auto")
+
+
 @pytest.mark.parametrize("name", golden_cases())
-def test_golden_fixtures_all_families(cuda, name):
+def test_golden_fixtures_all_families(cuda, pairing, name):
     shape, x, w, b, y = load_golden(name)
     fams = _families(shape)
     assert "generic" in fams
@@ -52,7 +61,7 @@ def _reduced(shape, max_ops=3e10):
 
 
 @pytest.mark.parametrize("case", m.BASELINE_CASES)
-def test_baseline_configs_full_compare(cuda, case):
+def test_baseline_configs_full_compare(cuda, pairing, case):
     shape = _reduced(m.load_workloads()[case])
     x, w, b = m.make_inputs(shape)
     want = pyoracle.conv(shape, x, w, b)
@@ -140,7 +149,7 @@ def _random_shapes(count, seed=2026):
 
 
 @pytest.mark.parametrize("idx,shape", list(enumerate(_random_shapes(40))))
-def test_random_shapes(cuda, idx, shape):
+def test_random_shapes(cuda, pairing, idx, shape):
     x, w, b = m.make_inputs(shape, seed=idx)
     want = pyoracle.conv(shape, x, w, b)
     for fam in _families(shape):
@@ -185,7 +194,7 @@ def test_ineligible_and_bad_pointer_statuses(cuda):
     assert st == _abi.BAD_POINTER
 
 
-def test_device_wait_timeout_is_reported_and_context_survives(cuda):
+def test_device_wait_timeout_is_reported_and_context_survives(cuda, pairing):
     # Failure detection without a GPU fault: the producer is told to issue no
     # copies, every consumer wait runs out after 20 ms, the kernel unwinds
     # (TMEM released, nothing in flight) and the host reads DEVICE_TIMEOUT.
