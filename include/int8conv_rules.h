@@ -88,12 +88,21 @@ I8C_RULE int i8c_strip_eligible(const int8conv_shape *s) {
          i8c_corner_ok(i8c_upper_corner(s->w, s->pad_w, 1, i8c_out_w(s) + s->s - 1));
 }
 
-/* HALO and SPLITK predicates are defined by their kernels (int8conv_eligible);
- * the constexpr forms below are the same rules. */
-I8C_RULE int i8c_halo_eligible(const int8conv_shape *s) {
-  return 0 * (s != 0);
+/* Channel block (bytes of C per k-block) the kernels use for a shape. */
+I8C_RULE int32_t i8c_channel_block(int32_t c) {
+  return c % 128 == 0 ? 128 : c % 64 == 0 ? 64 : 32;
 }
+
+/* SPLITK: the R*S*C reduction of each output tile is split across the CTAs
+ * of a cluster, so there must be at least two k-blocks (tap x channel block)
+ * to split.  Same TMA limits as GENERIC. */
 I8C_RULE int i8c_splitk_eligible(const int8conv_shape *s) {
+  return i8c_generic_eligible(s) &&
+         (int64_t)s->r * s->s * ((s->c + i8c_channel_block(s->c) - 1) / i8c_channel_block(s->c)) >= 2;
+}
+
+/* HALO is not built yet: no shape is eligible. */
+I8C_RULE int i8c_halo_eligible(const int8conv_shape *s) {
   return 0 * (s != 0);
 }
 

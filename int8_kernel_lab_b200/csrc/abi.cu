@@ -22,7 +22,8 @@ bool aligned16(const void *p) { return p != nullptr && (reinterpret_cast<uintptr
 // The kernel families implemented in this build.  A family whose kernel is
 // not built reports every shape as ineligible.
 bool family_built(int strategy) {
-  return strategy == INT8CONV_GENERIC || strategy == INT8CONV_STRIP;
+  return strategy == INT8CONV_GENERIC || strategy == INT8CONV_STRIP ||
+         strategy == INT8CONV_SPLITK;
 }
 
 int8conv_status launch_family(int strategy, const int8conv_shape *shape, const int8_t *input,
@@ -45,6 +46,8 @@ int8conv_status launch_family(int strategy, const int8conv_shape *shape, const i
       return i8c::launch_generic_impl(*shape, input, filter, bias, output, st);
     case INT8CONV_STRIP:
       return i8c::launch_strip_impl(*shape, input, filter, bias, output, st);
+    case INT8CONV_SPLITK:
+      return i8c::launch_splitk_impl(*shape, input, filter, bias, output, st);
     default:
       return INT8CONV_NOT_ELIGIBLE;
   }

@@ -27,6 +27,7 @@ struct ConvGeom {
   int32_t acc_stride;// TMEM columns between the two accumulator buffers
   int32_t tmem_cols; // TMEM columns allocated (power of two)
   int32_t pair;      // 1: cta_group::2 CTA pairs, 256-row tiles
+  int32_t tma_store; // 1: epilogue writes 32x32 blocks with TMA tensor stores
   int32_t stages;    // shared-memory ring depth (B ring; also A for GENERIC)
   int32_t m_tiles, n_tiles, num_tiles;
   // STRIP only: the M dimension runs over padded-row positions

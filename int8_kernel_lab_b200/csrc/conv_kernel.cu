@@ -68,7 +68,8 @@ struct SwizzleOf<32> {
   static constexpr Layout kLayout = Layout::kSw32;
 };
 
-constexpr uint32_t kEpilogueStaging = 4 * 32 * 128;
+// Epilogue staging: 4 warps x 2 buffers x (32 rows x 128 B).
+constexpr uint32_t kEpilogueStaging = 4 * 2 * 32 * 128;
 constexpr uint32_t kOneCtaPerSm = kMaxSmem / 2 + 1024;
 
 // Shared-memory plan, identical on host and device.
@@ -85,7 +86,9 @@ __host__ __device__ inline SmemPlan smem_plan(int cblk, int b_rows, int a_rows, 
   p.b_bytes = b_rows * cblk;
   p.a_off = 0;
   p.b_off = p.a_off + a_stages * p.a_bytes;
-  p.stage_off = p.b_off + b_stages * p.b_bytes;  // epilogue staging, 4 warps x 32 x 128 B
+  // Epilogue staging starts on a 1024-byte boundary: it doubles as the
+  // 128-byte-swizzled source of the TMA output stores.
+  p.stage_off = (p.b_off + b_stages * p.b_bytes + 1023) & ~1023u;
   p.bar_off = p.stage_off + kEpilogueStaging;
   // a_full/a_empty[a_stages], b_full/b_empty[b_stages], tfull[2], tempty[2], drain, slot
   const uint32_t bar_bytes = (2 * a_stages + 2 * b_stages + 5) * 8 + 8;
@@ -122,7 +125,8 @@ __device__ __forceinline__ void commit_to(uint64_t *bar) {
 template <int CBLK, bool STRIP, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_kernel(const __grid_constant__ CUtensorMap tmap_x,
-                const __grid_constant__ CUtensorMap tmap_w, const ConvGeom g,
+                const __grid_constant__ CUtensorMap tmap_w,
+                const __grid_constant__ CUtensorMap tmap_y, const ConvGeom g,
                 const int32_t *__restrict__ bias, int32_t *__restrict__ out, const RunCtl ctl) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment: the SW128 atom (8 rows x 128 B) starts on it.  The
@@ -404,6 +408,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         PAIR ? mapa_shared(smem_u32(&tempty[1]), 0) : smem_u32(&tempty[1]);
     int acc = 0;
     uint32_t acc_phase = 0;
+    // Staging buffers alternate by a block counter that runs across tiles, so
+    // consecutive stores never share a buffer even when BN/32 is odd.
+    int ci = 0;
     for (int tile = tile_first; tile < g.num_tiles; tile += tile_step) {
       const int m_tile = tile / g.n_tiles;
       const int n_tile = tile - m_tile * g.n_tiles;
@@ -427,22 +434,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * g.acc_stride;
       // Each 32x32 int32 block (this warp's 32 rows x 32 columns) goes through
-      // swizzled shared memory so the global stores are whole 128-byte row
-      // segments: thread-per-row stores would issue one L2 request per 16 B.
-      int4 *stg = staging + (warp - 2) * 32 * 8;
+      // shared memory, swizzled by 16-byte chunk ^ (row & 7): the 128-byte TMA
+      // swizzle.  Thread-per-row global stores would issue one L2 request per
+      // 16 B; instead the block leaves as one TMA tensor store (rows >= M and
+      // columns >= K clipped by the TMA unit), or, where that does not apply,
+      // as 16-byte stores that write whole 128-byte row segments.
+      int4 *stg_w = staging + (warp - 2) * 2 * 256;
       const int q = lane & 7;    // 16-byte column group this lane stores
       const int rsub = lane >> 3;
-      for (int c0 = 0; c0 < g.bn; c0 += 32) {
+      const int row0 = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + quarter * 32;
+      for (int c0 = 0; c0 < g.bn; c0 += 32, ++ci) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + c0, v);
         tmem_ld_wait();
+        if (c0 + 32 >= g.bn) {
+          // Last read of this accumulator: hand it back to the MMA issuer now.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (PAIR)
+              mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+            else
+              mbar_arrive(&tempty[acc]);
+          }
+        }
+        const int col0 = n0 + c0;
+        if (g.tma_store) {
+          int4 *stg = stg_w + (ci & 1) * 256;
+          // The store issued two blocks ago read this buffer: let it finish.
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const bool in = c0 + 4 * j < g.bn && col0 + 4 * j < g.K;
+            const int4 bb =
+                in ? __ldg(reinterpret_cast<const int4 *>(bias + col0) + j) : make_int4(0, 0, 0, 0);
+            stg[lane * 8 + (j ^ (lane & 7))] = make_int4(
+                static_cast<int32_t>(v[4 * j]) + bb.x, static_cast<int32_t>(v[4 * j + 1]) + bb.y,
+                static_cast<int32_t>(v[4 * j + 2]) + bb.z, static_cast<int32_t>(v[4 * j + 3]) + bb.w);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_y, stg, col0, row0);
+            bulk_commit_group();
+          }
+          continue;
+        }
+        int4 *stg = stg_w;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           stg[lane * 8 + (j ^ (lane & 7))] =
               make_int4(static_cast<int32_t>(v[4 * j]), static_cast<int32_t>(v[4 * j + 1]),
                         static_cast<int32_t>(v[4 * j + 2]), static_cast<int32_t>(v[4 * j + 3]));
         __syncwarp();
-        const int col0 = n0 + c0;
         if (vec_k) {
           // K % 4 == 0: 16-byte groups are wholly inside or outside [0, K).
           const bool col_ok = c0 + 4 * q < g.bn && col0 + 4 * q < g.K;
@@ -476,19 +521,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if constexpr (PAIR)
-          mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
-        else
-          mbar_arrive(&tempty[acc]);
-      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
+    // Output stores still reading shared memory or in flight finish first.
+    if (g.tma_store && lane == 0) bulk_wait_group_all();
   }
 
   tc_fence_before();
@@ -593,6 +632,10 @@ static bool plan_geometry(const int8conv_shape &s, bool strip, bool pair, ConvGe
   g.m_tiles = static_cast<int32_t>((positions + tile_rows - 1) / tile_rows);
   g.n_tiles = (s.k + g.bn - 1) / g.bn;
   g.num_tiles = g.m_tiles * g.n_tiles;
+  // TMA output stores: GENERIC rows are contiguous in NHWK; the row pitch
+  // 4*K must be a multiple of 16 bytes; a 32-column block must not reach into
+  // the next N tile (columns >= K are clipped, columns of a neighbour are not).
+  g.tma_store = !strip && s.k % 4 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
   return true;
 }
 
@@ -601,7 +644,7 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
                                 const int8_t *w, const int32_t *b, int32_t *y,
                                 cudaStream_t stream) {
   DeviceInfo &dev = device_info();
-  CUtensorMap maps[2];
+  CUtensorMap maps[3];
   const int pixels = STRIP ? g.strip_px : kBlockM;
   const int count_w = STRIP ? g.Wp : g.Q;
   const int b_rows = PAIR ? g.bn / 2 : g.bn;
@@ -609,6 +652,11 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   if (st != INT8CONV_OK) return st;
   st = filter_map_tiled(s, w, CBLK, b_rows, &maps[1]);
   if (st != INT8CONV_OK) return st;
+  maps[2] = CUtensorMap{};
+  if (g.tma_store) {
+    st = output_map_tiled(y, g.M, g.K, &maps[2]);
+    if (st != INT8CONV_OK) return st;
+  }
   const SmemPlan plan = smem_plan(CBLK, b_rows, STRIP ? g.a_rows : kBlockM, g.a_stages, g.stages);
   auto kernel = conv_kernel<CBLK, STRIP, PAIR>;
   // At least half an SM's shared memory: one CTA per SM, so a CTA never waits
@@ -632,10 +680,10 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], g, b, y, ctl);
+    err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], g, b, y, ctl);
   } else {
     const int grid = g.num_tiles < dev.sm_count ? g.num_tiles : dev.sm_count;
-    kernel<<<grid, kThreads, smem_bytes, stream>>>(maps[0], maps[1], g, b, y, ctl);
+    kernel<<<grid, kThreads, smem_bytes, stream>>>(maps[0], maps[1], maps[2], g, b, y, ctl);
     err = cudaGetLastError();
   }
   note_launch();
@@ -656,7 +704,10 @@ static int8conv_status launch_cblk(const int8conv_shape &s, const ConvGeom &g, i
   }
 }
 
-// CTA pairs pay off once there are enough 256-row tiles to fill every SM.
+// CTA pairs halve the filter bytes per output row.  Measured on B200 they pay
+// off when the filter tile is the full 256 columns and there are at least two
+// waves of 256-row tiles (5a: 357 vs 403 us, 5b: 92 vs 102 us); narrower or
+// smaller layers run faster as single CTAs (3b: 17 vs 23 us, 2: 17 vs 20 us).
 static bool use_pair(const int8conv_shape &s, bool strip) {
   const int mode = pairing_mode();
   if (mode == 1) return false;
@@ -664,7 +715,7 @@ static bool use_pair(const int8conv_shape &s, bool strip) {
   int cblk = 0;
   if (!plan_geometry(s, strip, true, g, cblk)) return false;
   if (mode == 2) return true;
-  return g.num_tiles >= device_info().sm_count / 2;
+  return g.bn == 256 && g.num_tiles >= device_info().sm_count;
 }
 
 template <bool STRIP>

@@ -48,10 +48,16 @@ int8conv_status activation_map_im2col(const int8conv_shape &s, const int8_t *x, 
 int8conv_status filter_map_tiled(const int8conv_shape &s, const int8_t *w, int channels,
                                  int rows, CUtensorMap *map);
 
+// Tiled tensor map over the NHWK int32 output viewed as [M][K], box 32 x 32,
+// 128-byte swizzle (the epilogue's staging layout).
+int8conv_status output_map_tiled(int32_t *y, int64_t m, int k, CUtensorMap *map);
+
 // Family launchers (valid, eligible shape; pointers already checked).
 int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                     const int32_t *b, int32_t *y, cudaStream_t stream);
 int8conv_status launch_strip_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                   const int32_t *b, int32_t *y, cudaStream_t stream);
+int8conv_status launch_splitk_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                   const int32_t *b, int32_t *y, cudaStream_t stream);
 
 }  // namespace i8c
