@@ -80,8 +80,21 @@ int int8conv_eligible(const int8conv_shape *shape, int strategy) {
 }
 
 int int8conv_select(const int8conv_shape *shape) {
-  // B200 dispatch policy (measured): strip where eligible, else generic.
-  if (int8conv_eligible(shape, INT8CONV_STRIP)) return INT8CONV_STRIP;
+  // B200 dispatch policy, from conv_lab sweeps on B200:
+  //  * GENERIC (with CTA pairs where they pay off) wins every large layer;
+  //    STRIP's strip reuse no longer pays once the epilogue uses TMA stores
+  //    (5a 357 vs 396 us, 5c 39 vs 51 us).
+  //  * SPLITK when the layer has too few 128-row output tiles to occupy half
+  //    the GPU but a reduction deep enough to split (7x7 and 14x14 layers).
+  if (!i8c_shape_valid(shape)) return INT8CONV_GENERIC;
+  const int64_t m = static_cast<int64_t>(shape->n) * i8c_out_h(shape) * i8c_out_w(shape);
+  const int64_t n_tiles = (shape->k + 255) / 256;
+  const int64_t tiles = (m + 127) / 128 * n_tiles;
+  const int32_t cblk = i8c_channel_block(shape->c);
+  const int64_t kblocks =
+      static_cast<int64_t>(shape->r) * shape->s * ((shape->c + cblk - 1) / cblk);
+  if (int8conv_eligible(shape, INT8CONV_SPLITK) && tiles < 74 && kblocks >= 8)
+    return INT8CONV_SPLITK;
   return INT8CONV_GENERIC;
 }
 

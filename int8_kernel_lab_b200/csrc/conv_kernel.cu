@@ -47,6 +47,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "conv_common.h"
 #include "launch.h"
 #include "sm100.cuh"
@@ -662,8 +664,14 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   // At least half an SM's shared memory: one CTA per SM, so a CTA never waits
   // for another's TMEM columns.
   const uint32_t smem_bytes = plan.total > kOneCtaPerSm ? plan.total : kOneCtaPerSm;
-  if (!ensure_smem_attr(reinterpret_cast<const void *>(kernel), smem_bytes))
-    return INT8CONV_CUDA_ERROR;
+  // The opt-in shared-memory limit is set once per device and instantiation.
+  static std::atomic<uint32_t> smem_set[64];
+  std::atomic<uint32_t> &slot = smem_set[dev.device & 63];
+  if (slot.load(std::memory_order_relaxed) < smem_bytes) {
+    if (!ensure_smem_attr(reinterpret_cast<const void *>(kernel), kMaxSmem))
+      return INT8CONV_CUDA_ERROR;
+    slot.store(kMaxSmem, std::memory_order_relaxed);
+  }
   const RunCtl ctl = run_ctl();
   cudaError_t err;
   if constexpr (PAIR) {

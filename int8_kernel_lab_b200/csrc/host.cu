@@ -59,26 +59,33 @@ struct MapEntry {
   CUtensorMap map;
   bool used;
 };
-constexpr int kMapCache = 128;
+// Direct-mapped by an FNV-1a hash of the key: a hit costs one comparison.
+constexpr int kMapCache = 512;
 MapEntry g_maps[kMapCache];
-int g_map_next = 0;
 std::mutex g_map_mutex;
 
+uint32_t key_slot(const MapKey &key) {
+  const unsigned char *p = reinterpret_cast<const unsigned char *>(&key);
+  uint32_t h = 2166136261u;
+  for (size_t i = 0; i < sizeof(MapKey); ++i) h = (h ^ p[i]) * 16777619u;
+  return h % kMapCache;
+}
+
 bool map_lookup(const MapKey &key, CUtensorMap *map) {
+  const uint32_t slot = key_slot(key);
   std::lock_guard<std::mutex> lock(g_map_mutex);
-  for (int i = 0; i < kMapCache; ++i) {
-    if (g_maps[i].used && memcmp(&g_maps[i].key, &key, sizeof(MapKey)) == 0) {
-      *map = g_maps[i].map;
-      return true;
-    }
+  const MapEntry &e = g_maps[slot];
+  if (e.used && memcmp(&e.key, &key, sizeof(MapKey)) == 0) {
+    *map = e.map;
+    return true;
   }
   return false;
 }
 
 void map_store(const MapKey &key, const CUtensorMap &map) {
+  const uint32_t slot = key_slot(key);
   std::lock_guard<std::mutex> lock(g_map_mutex);
-  MapEntry &e = g_maps[g_map_next];
-  g_map_next = (g_map_next + 1) % kMapCache;
+  MapEntry &e = g_maps[slot];
   e.key = key;
   e.map = map;
   e.used = true;

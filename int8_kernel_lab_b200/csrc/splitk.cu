@@ -19,6 +19,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "conv_common.h"
 #include "launch.h"
 #include "sm100.cuh"
@@ -344,7 +346,13 @@ static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &
   const uint32_t total = 1024 + sg.ring_bytes + (2 * sg.g.stages + 1) * 8 + 16;
   const uint32_t smem = total > kMaxSmem / 2 + 1024 ? total : kMaxSmem / 2 + 1024;
   auto kernel = splitk_kernel<CBLK>;
-  if (!ensure_smem_attr(reinterpret_cast<const void *>(kernel), smem)) return INT8CONV_CUDA_ERROR;
+  static std::atomic<uint32_t> smem_set[64];
+  std::atomic<uint32_t> &slot = smem_set[device_info().device & 63];
+  if (slot.load(std::memory_order_relaxed) < smem) {
+    if (!ensure_smem_attr(reinterpret_cast<const void *>(kernel), kMaxSmem))
+      return INT8CONV_CUDA_ERROR;
+    slot.store(kMaxSmem, std::memory_order_relaxed);
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sg.g.num_tiles * sg.splits, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
