@@ -134,6 +134,26 @@ int8conv_status int8conv_launch_splitk(const int8conv_shape *shape,
                                        void *workspace, size_t workspace_bytes,
                                        void *stream);
 
+/* ---- host buffers ------------------------------------------------------------*/
+
+/* End-to-end convolution of HOST buffers (no reference counterpart; the
+ * reference copies synchronously around each launch, src/conv_lab.cu:163-168,
+ * :190-192).  Copies the filter and bias, then streams the batch through the
+ * GPU in `chunks` groups of whole images: the host->device copy of group i+1,
+ * the convolution of group i and the device->host copy of group i-1 overlap
+ * on separate streams.  The device buffers are the caller's and hold the full
+ * tensors; pinned host memory is needed for the copies to overlap.  Returns
+ * after enqueueing: `stream` waits for every copy and launch, so synchronising
+ * it (or any later work on it) sees the finished host output.  The chunk
+ * launches run strategy `strategy` (or the dispatch policy for INT8CONV_AUTO)
+ * on each group's shape. */
+int8conv_status int8conv_launch_host(int strategy, const int8conv_shape *shape,
+                                     const int8_t *host_input, const int8_t *host_filter,
+                                     const int32_t *host_bias, int32_t *host_output,
+                                     int8_t *dev_input, int8_t *dev_filter,
+                                     int32_t *dev_bias, int32_t *dev_output,
+                                     int chunks, void *stream);
+
 /* ---- device status ---------------------------------------------------------*/
 
 /* Synchronises the current device and returns INT8CONV_DEVICE_TIMEOUT if any

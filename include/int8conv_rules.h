@@ -101,9 +101,20 @@ I8C_RULE int i8c_splitk_eligible(const int8conv_shape *s) {
          (int64_t)s->r * s->s * ((s->c + i8c_channel_block(s->c) - 1) / i8c_channel_block(s->c)) >= 2;
 }
 
-/* HALO is not built yet: no shape is eligible. */
+/* HALO: positions run over the zero-padded image (Hp x Wp, Hp = out_h +
+ * (R-1)*dh, Wp = out_w + (S-1)*dw); one staged halo tile of
+ * 128 + (R-1)*dh*Wp + (S-1)*dw pixels per channel block feeds all R*S taps.
+ * Needs unit strides and a staged tile of at most 512 pixels (small spatial
+ * layers). */
 I8C_RULE int i8c_halo_eligible(const int8conv_shape *s) {
-  return 0 * (s != 0);
+  return i8c_generic_eligible(s) && s->stride_h == 1 && s->stride_w == 1 &&
+         128 + (int64_t)(s->r - 1) * s->dilation_h *
+                   (i8c_out_w(s) + (int64_t)(s->s - 1) * s->dilation_w) +
+                 (int64_t)(s->s - 1) * s->dilation_w <= 512 &&
+         i8c_corner_ok(i8c_upper_corner(s->w, s->pad_w, 1,
+                                        i8c_out_w(s) + (s->s - 1) * s->dilation_w)) &&
+         i8c_corner_ok(i8c_upper_corner(s->h, s->pad_h, 1,
+                                        i8c_out_h(s) + (s->r - 1) * s->dilation_h));
 }
 
 I8C_RULE int i8c_eligible(const int8conv_shape *s, int strategy) {

@@ -66,6 +66,7 @@ SIGNATURES = {
     "int8conv_launch_spatial_strip": (ctypes.c_int, [_SP, _P, _P, _P, _P, _P]),
     "int8conv_launch_halo": (ctypes.c_int, [_SP, _P, _P, _P, _P, _P]),
     "int8conv_launch_splitk": (ctypes.c_int, [_SP, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    "int8conv_launch_host": (ctypes.c_int, [ctypes.c_int, _SP] + [_P] * 8 + [ctypes.c_int, _P]),
     "int8conv_device_status": (ctypes.c_int, []),
     "int8conv_set_wait_limit_ns": (None, [ctypes.c_uint64]),
     "int8conv_debug_starve_producer": (None, [ctypes.c_int]),

@@ -108,6 +108,30 @@ def conv2d(shape: ConvShape, x, w, b, strategy: str = "auto", stream=None):
     return y
 
 
+def launch_host(strategy: str, shape: ConvShape, hx, hw, hb, hy, dx, dw, db, dy, *,
+                chunks: int = 8, stream=None) -> None:
+    """int8conv_launch_host: convolve HOST tensors (pinned CPU tensors for
+    overlap) through caller-owned device buffers, streaming the batch in
+    `chunks` groups of images so the PCIe copies in both directions overlap the
+    kernels.  Asynchronous on `stream`; synchronise it before reading `hy`."""
+    import torch
+
+    for name, t, dev in (("hx", hx, False), ("hw", hw, False), ("hb", hb, False),
+                         ("hy", hy, False), ("dx", dx, True), ("dw", dw, True),
+                         ("db", db, True), ("dy", dy, True)):
+        if t.is_cuda != dev or not t.is_contiguous():
+            where = "CUDA" if dev else "host"
+            raise ValueError(f"{name}: expected a contiguous {where} tensor")
+    _check_tensors(shape, dx, dw, db, dy)
+    if (hx.numel() != shape.input_elements or hw.numel() != shape.filter_elements
+            or hb.numel() != shape.k or hy.numel() != shape.output_elements):
+        raise ValueError("host tensor sizes do not match the shape")
+    status = _abi.lib.int8conv_launch_host(
+        _abi.STRATEGIES[strategy], shape.c_struct(), _ptr(hx), _ptr(hw), _ptr(hb), _ptr(hy),
+        _ptr(dx), _ptr(dw), _ptr(db), _ptr(dy), int(chunks), _stream(stream))
+    _abi.check(status, f"{strategy} host launch of {shape}")
+
+
 def device_status() -> int:
     """int8conv_device_status(): synchronises; DEVICE_TIMEOUT if a bounded wait ran out."""
     return int(_abi.lib.int8conv_device_status())

@@ -22,8 +22,7 @@ bool aligned16(const void *p) { return p != nullptr && (reinterpret_cast<uintptr
 // The kernel families implemented in this build.  A family whose kernel is
 // not built reports every shape as ineligible.
 bool family_built(int strategy) {
-  return strategy == INT8CONV_GENERIC || strategy == INT8CONV_STRIP ||
-         strategy == INT8CONV_SPLITK;
+  return strategy >= INT8CONV_GENERIC && strategy < INT8CONV_NUM_STRATEGIES;
 }
 
 int8conv_status launch_family(int strategy, const int8conv_shape *shape, const int8_t *input,
@@ -46,6 +45,8 @@ int8conv_status launch_family(int strategy, const int8conv_shape *shape, const i
       return i8c::launch_generic_impl(*shape, input, filter, bias, output, st);
     case INT8CONV_STRIP:
       return i8c::launch_strip_impl(*shape, input, filter, bias, output, st);
+    case INT8CONV_HALO:
+      return i8c::launch_halo_impl(*shape, input, filter, bias, output, st);
     case INT8CONV_SPLITK:
       return i8c::launch_splitk_impl(*shape, input, filter, bias, output, st);
     default:
@@ -177,6 +178,27 @@ int8conv_status int8conv_launch_splitk(const int8conv_shape *shape, const int8_t
                                        void *stream) {
   return launch_family(INT8CONV_SPLITK, shape, input, filter, bias, output, workspace,
                        workspace_bytes, stream);
+}
+
+int8conv_status int8conv_launch_host(int strategy, const int8conv_shape *shape,
+                                     const int8_t *host_input, const int8_t *host_filter,
+                                     const int32_t *host_bias, int32_t *host_output,
+                                     int8_t *dev_input, int8_t *dev_filter, int32_t *dev_bias,
+                                     int32_t *dev_output, int chunks, void *stream) {
+  if (!i8c_shape_valid(shape)) return INT8CONV_BAD_SHAPE;
+  if (strategy != INT8CONV_AUTO && (strategy < 0 || strategy >= INT8CONV_NUM_STRATEGIES))
+    return INT8CONV_BAD_ARGUMENT;
+  if (chunks < 1) return INT8CONV_BAD_ARGUMENT;
+  if (strategy != INT8CONV_AUTO && !int8conv_eligible(shape, strategy))
+    return INT8CONV_NOT_ELIGIBLE;
+  if (!host_input || !host_filter || !host_bias || !host_output || !aligned16(dev_input) ||
+      !aligned16(dev_filter) || !aligned16(dev_bias) || !aligned16(dev_output))
+    return INT8CONV_BAD_POINTER;
+  const int8conv_status dev = i8c::check_device();
+  if (dev != INT8CONV_OK) return dev;
+  return i8c::launch_host_pipeline(strategy, *shape, host_input, host_filter, host_bias,
+                                   host_output, dev_input, dev_filter, dev_bias, dev_output,
+                                   chunks, static_cast<cudaStream_t>(stream));
 }
 
 int8conv_status int8conv_device_status(void) {

@@ -30,15 +30,16 @@ struct ConvGeom {
   int32_t tma_store; // 1: epilogue writes 32x32 blocks with TMA tensor stores
   int32_t stages;    // shared-memory ring depth (B ring; also A for GENERIC)
   int32_t m_tiles, n_tiles, num_tiles;
-  // STRIP only: the M dimension runs over padded-row positions
-  // (n, oy, j) with j in [0, Wp), Wp = out_w + S - 1; positions j >= out_w
-  // are computed and discarded.
+  // STRIP / HALO: the M dimension runs over padded-grid positions
+  // (n, i, j), j in [0, Wp), i in [0, rows); positions with j >= out_w or
+  // i >= out_h are computed and discarded.
   int32_t Wp;        // padded row width
-  int32_t PWp;       // out_h * Wp
+  int32_t rows;      // padded-grid rows per image (out_h for STRIP, Hp for HALO)
+  int32_t PWp;       // rows * Wp
   int32_t Mp;        // n * out_h * Wp
-  int32_t strip_px;  // pixels per strip load (128 + S - 1)
-  int32_t a_rows;    // rows reserved per strip stage (strip_px rounded up to 8)
-  int32_t a_stages;  // strip ring depth
+  int32_t strip_px;  // pixels per staged load (128 + largest tap shift)
+  int32_t a_rows;    // rows reserved per staged tile (strip_px rounded up to 8)
+  int32_t a_stages;  // staged-tile ring depth
 };
 
 // Failure-detection controls passed to every kernel.

@@ -74,6 +74,14 @@ struct SwizzleOf<32> {
 constexpr uint32_t kEpilogueStaging = 4 * 2 * 32 * 128;
 constexpr uint32_t kOneCtaPerSm = kMaxSmem / 2 + 1024;
 
+// Kernel variants: how the A operand (output pixels x channels) is staged.
+constexpr int kModeGeneric = 0;  // one im2col tile per tap and channel block
+constexpr int kModeStrip = 1;    // one row strip per (filter row, channel block)
+constexpr int kModeHalo = 2;     // one halo tile per channel block
+// Largest staged tile (rows of CBLK bytes): im2col loads move at most 1024
+// pixels, and a few stages must fit in shared memory.
+constexpr int kMaxStagedRows = 512;
+
 // Shared-memory plan, identical on host and device.
 struct SmemPlan {
   uint32_t a_bytes, b_bytes;  // one stage of A / B (this CTA's share)
@@ -124,7 +132,7 @@ __device__ __forceinline__ void commit_to(uint64_t *bar) {
     umma_commit(bar);
 }
 
-template <int CBLK, bool STRIP, bool PAIR>
+template <int CBLK, int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_w,
@@ -136,8 +144,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   constexpr int kTileRows = PAIR ? 2 * kBlockM : kBlockM;
-  const int a_stages = STRIP ? g.a_stages : g.stages;
-  const int a_rows = STRIP ? g.a_rows : kBlockM;
+  constexpr bool STRIP = MODE == kModeStrip;
+  constexpr bool HALO = MODE == kModeHalo;
+  constexpr bool SHIFT = STRIP || HALO;  // A operand = shifted views of one staged tile
+  const int a_stages = SHIFT ? g.a_stages : g.stages;
+  const int a_rows = SHIFT ? g.a_rows : kBlockM;
   const int b_rows = PAIR ? g.bn / 2 : g.bn;
   const SmemPlan plan = smem_plan(CBLK, b_rows, a_rows, a_stages, g.stages);
   uint8_t *a_ring = smem + plan.a_off;
@@ -155,8 +166,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtx wctx{ctl.wait_ns, ctl.status};
-  const int m_span = STRIP ? g.PWp : g.PQ;     // positions per image
-  const int m_row = STRIP ? g.Wp : g.Q;        // positions per output row
+  const int m_span = SHIFT ? g.PWp : g.PQ;     // positions per image
+  const int m_row = SHIFT ? g.Wp : g.Q;        // positions per output row
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const bool leader = rank == 0;
   const int tile_first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
@@ -202,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer ----------------
       Ring ra, rb;
       long armed_a = 0, armed_b = 0;
-      const uint32_t a_tx = (STRIP ? g.strip_px : kBlockM) * CBLK;
+      const uint32_t a_tx = (SHIFT ? g.strip_px : kBlockM) * CBLK;
       const uint32_t b_tx = plan.b_bytes;
       // A pair credits all bytes to the leader's barriers, armed for both CTAs.
       const uint32_t tx_mult = PAIR ? 2u : 1u;
@@ -221,47 +232,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = rem - p * m_row;
         const int x_w = q * g.stride_w - g.pad_w;
         const int x_h = p * g.stride_h - g.pad_h;
-        if constexpr (STRIP) {
-          for (int r = 0; r < g.R && ok; ++r) {
-            for (int cb = 0; cb < g.cblocks && ok; ++cb) {
-              if (!mbar_wait(&a_empty[ra.stage], ra.phase ^ 1u, wctx, kStatusTimeoutEmpty)) {
+        if constexpr (SHIFT) {
+          // STRIP: one staged row strip per (filter row r, channel block),
+          //   shared by the S filter columns.
+          // HALO: one staged halo tile per channel block, shared by all R*S taps.
+          const int groups = STRIP ? g.R * g.cblocks : g.cblocks;
+          const int taps = STRIP ? g.S : g.R * g.S;
+          for (int grp = 0; grp < groups && ok; ++grp) {
+            const int ra_row = STRIP ? grp / g.cblocks : 0;
+            const int cb = STRIP ? grp - ra_row * g.cblocks : grp;
+            if (!mbar_wait(&a_empty[ra.stage], ra.phase ^ 1u, wctx, kStatusTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            if (!ctl.starve) {
+              if (leader) {
+                mbar_arrive_expect_tx(&a_full[ra.stage], tx_mult * a_tx);
+                ++armed_a;
+              }
+              void *dst = a_ring + ra.stage * plan.a_bytes;
+              const uint16_t oh = static_cast<uint16_t>(ra_row * g.dil_h);
+              if constexpr (PAIR)
+                tma_load_im2col_4d_pair(dst, &tmap_x, full_addr(&a_full[ra.stage]), cb * CBLK,
+                                        x_w, x_h, img, 0, oh);
+              else
+                tma_load_im2col_4d(dst, &tmap_x, &a_full[ra.stage], cb * CBLK, x_w, x_h, img, 0,
+                                   oh);
+            }
+            ra.next(a_stages);
+            for (int t = 0; t < taps; ++t) {
+              const int tap = STRIP ? ra_row * g.S + t : t;
+              if (!mbar_wait(&b_empty[rb.stage], rb.phase ^ 1u, wctx, kStatusTimeoutEmpty)) {
                 ok = false;
                 break;
               }
               if (!ctl.starve) {
                 if (leader) {
-                  mbar_arrive_expect_tx(&a_full[ra.stage], tx_mult * a_tx);
-                  ++armed_a;
+                  mbar_arrive_expect_tx(&b_full[rb.stage], tx_mult * b_tx);
+                  ++armed_b;
                 }
-                void *dst = a_ring + ra.stage * plan.a_bytes;
-                const uint16_t oh = static_cast<uint16_t>(r * g.dil_h);
+                void *dst = b_ring + rb.stage * plan.b_bytes;
                 if constexpr (PAIR)
-                  tma_load_im2col_4d_pair(dst, &tmap_x, full_addr(&a_full[ra.stage]), cb * CBLK,
-                                          x_w, x_h, img, 0, oh);
+                  tma_load_3d_pair(dst, &tmap_w, full_addr(&b_full[rb.stage]), cb * CBLK, tap, n0);
                 else
-                  tma_load_im2col_4d(dst, &tmap_x, &a_full[ra.stage], cb * CBLK, x_w, x_h, img,
-                                     0, oh);
+                  tma_load_3d(dst, &tmap_w, &b_full[rb.stage], cb * CBLK, tap, n0);
               }
-              ra.next(a_stages);
-              for (int s = 0; s < g.S; ++s) {
-                if (!mbar_wait(&b_empty[rb.stage], rb.phase ^ 1u, wctx, kStatusTimeoutEmpty)) {
-                  ok = false;
-                  break;
-                }
-                if (!ctl.starve) {
-                  if (leader) {
-                    mbar_arrive_expect_tx(&b_full[rb.stage], tx_mult * b_tx);
-                    ++armed_b;
-                  }
-                  void *dst = b_ring + rb.stage * plan.b_bytes;
-                  if constexpr (PAIR)
-                    tma_load_3d_pair(dst, &tmap_w, full_addr(&b_full[rb.stage]), cb * CBLK,
-                                     r * g.S + s, n0);
-                  else
-                    tma_load_3d(dst, &tmap_w, &b_full[rb.stage], cb * CBLK, r * g.S + s, n0);
-                }
-                rb.next(g.stages);
-              }
+              rb.next(g.stages);
             }
           }
         } else {
@@ -336,14 +352,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * g.acc_stride);
         uint32_t accumulate = 0;
-        if constexpr (STRIP) {
-          for (int rc = 0; rc < g.R * g.cblocks && ok; ++rc) {
+        if constexpr (SHIFT) {
+          const int groups = STRIP ? g.R * g.cblocks : g.cblocks;
+          const int taps = STRIP ? g.S : g.R * g.S;
+          for (int grp = 0; grp < groups && ok; ++grp) {
             if (!mbar_wait(&a_full[ra.stage], ra.phase, wctx, kStatusTimeoutFull)) {
               ok = false;
               break;
             }
             const uint32_t a_addr = smem_u32(a_ring + ra.stage * plan.a_bytes);
-            for (int s = 0; s < g.S; ++s) {
+            for (int t = 0; t < taps; ++t) {
+              // Tap t reads the staged tile `shift` rows further on: filter
+              // column s for a strip; r*dh*Wp + s*dw for a halo tile.
+              const int shift =
+                  STRIP ? t : (t / g.S) * g.dil_h * g.Wp + (t - (t / g.S) * g.S) * g.dil_w;
               if (!mbar_wait(&b_full[rb.stage], rb.phase, wctx, kStatusTimeoutFull)) {
                 ok = false;
                 break;
@@ -352,8 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint32_t b_addr = smem_u32(b_ring + rb.stage * plan.b_bytes);
 #pragma unroll
               for (int k = 0; k < CBLK / 32; ++k) {
-                // Filter column s reads the strip s rows further on.
-                mma(d_tmem, smem_desc(a_addr + s * CBLK + 32 * k, 16, kAtom, kLayout),
+                mma(d_tmem, smem_desc(a_addr + shift * CBLK + 32 * k, 16, kAtom, kLayout),
                     smem_desc(b_addr + 32 * k, 16, kAtom, kLayout), accumulate);
                 accumulate = 1;
               }
@@ -403,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
     const bool vec_k = (g.K & 3) == 0;
-    const int m_limit = STRIP ? g.Mp : g.M;
+    const int m_limit = SHIFT ? g.Mp : g.M;
     const uint32_t tempty_leader0 =
         PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
     const uint32_t tempty_leader1 =
@@ -420,13 +441,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = n_tile * g.bn;
       bool valid = pos < m_limit;
       int m = pos;
-      if constexpr (STRIP) {
+      if constexpr (SHIFT) {
+        // Padded-grid position (img, i, j): an output only for i < P, j < Q.
         const int img = pos / g.PWp;
         const int rem = pos - img * g.PWp;
-        const int p = rem / g.Wp;
-        const int j = rem - p * g.Wp;
-        valid = valid && j < g.Q;
-        m = (img * g.P + p) * g.Q + j;
+        const int i = rem / g.Wp;
+        const int j = rem - i * g.Wp;
+        valid = valid && j < g.Q && i < g.P;
+        m = (img * g.P + i) * g.Q + j;
       }
       // All lanes wait; the vote keeps the warp converged for tcgen05.ld even
       // if the wait runs out on some lanes only.
@@ -572,8 +594,7 @@ static int next_pow2(int v) {
 }
 
 // Fills the launch geometry; false if the shape does not fit the kernel.
-static bool plan_geometry(const int8conv_shape &s, bool strip, bool pair, ConvGeom &g,
-                          int &cblk) {
+static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, ConvGeom &g, int &cblk) {
   const int32_t out_h = (s.h + 2 * s.pad_h - s.dilation_h * (s.r - 1) - 1) / s.stride_h + 1;
   const int32_t out_w = (s.w + 2 * s.pad_w - s.dilation_w * (s.s - 1) - 1) / s.stride_w + 1;
   cblk = pick_cblk(s.c);
@@ -600,18 +621,28 @@ static bool plan_geometry(const int8conv_shape &s, bool strip, bool pair, ConvGe
   if (g.tmem_cols > 512) return false;
   const int tile_rows = pair ? 2 * kBlockM : kBlockM;
   const int b_bytes = (pair ? g.bn / 2 : g.bn) * cblk;
-  const int budget = kMaxSmem - 1024 - 512 - static_cast<int>(kEpilogueStaging);
+  // Shared memory left for the rings: minus the base alignment slack (1 KB),
+  // the staging buffer and its 1 KB alignment, and the barriers.
+  const int budget = kMaxSmem - 2048 - 512 - static_cast<int>(kEpilogueStaging);
   int64_t positions = g.M;
-  if (strip) {
-    g.Wp = out_w + s.s - 1;
-    g.PWp = out_h * g.Wp;
+  if (mode != kModeGeneric) {
+    // Padded grid: STRIP pads the row only (Wp = Q + S - 1, out_h rows);
+    // HALO pads both (Hp x Wp, every tap is a shift of one staged tile).
+    const bool halo = mode == kModeHalo;
+    g.Wp = out_w + (s.s - 1) * s.dilation_w;
+    g.rows = halo ? out_h + (s.r - 1) * s.dilation_h : out_h;
+    g.PWp = g.rows * g.Wp;
     positions = static_cast<int64_t>(s.n) * g.PWp;
     if (positions >= (int64_t(1) << 31)) return false;
     g.Mp = static_cast<int32_t>(positions);
-    g.strip_px = kBlockM + s.s - 1;
+    const int64_t shift = halo ? static_cast<int64_t>(s.r - 1) * s.dilation_h * g.Wp +
+                                     static_cast<int64_t>(s.s - 1) * s.dilation_w
+                               : s.s - 1;
+    if (kBlockM + shift > kMaxStagedRows) return false;
+    g.strip_px = static_cast<int32_t>(kBlockM + shift);
     g.a_rows = (g.strip_px + 7) / 8 * 8;
     const int a_bytes = g.a_rows * cblk;
-    // Strip ring: enough strips to keep S filter tiles per strip flowing.
+    // Ring of staged tiles: enough to keep the taps that share one flowing.
     g.a_stages = 3;
     int b_stages = (budget - g.a_stages * a_bytes) / b_bytes;
     if (b_stages > 12) b_stages = 12;
@@ -637,20 +668,22 @@ static bool plan_geometry(const int8conv_shape &s, bool strip, bool pair, ConvGe
   // TMA output stores: GENERIC rows are contiguous in NHWK; the row pitch
   // 4*K must be a multiple of 16 bytes; a 32-column block must not reach into
   // the next N tile (columns >= K are clipped, columns of a neighbour are not).
-  g.tma_store = !strip && s.k % 4 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
+  g.tma_store = mode == kModeGeneric && s.k % 4 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
   return true;
 }
 
-template <int CBLK, bool STRIP, bool PAIR>
+template <int CBLK, int MODE, bool PAIR>
 static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, const int8_t *x,
                                 const int8_t *w, const int32_t *b, int32_t *y,
                                 cudaStream_t stream) {
   DeviceInfo &dev = device_info();
   CUtensorMap maps[3];
-  const int pixels = STRIP ? g.strip_px : kBlockM;
-  const int count_w = STRIP ? g.Wp : g.Q;
+  constexpr bool SHIFT = MODE != kModeGeneric;
+  const int pixels = SHIFT ? g.strip_px : kBlockM;
+  const int count_w = SHIFT ? g.Wp : g.Q;
+  const int count_h = MODE == kModeHalo ? g.rows : g.P;
   const int b_rows = PAIR ? g.bn / 2 : g.bn;
-  int8conv_status st = activation_map_im2col(s, x, CBLK, pixels, count_w, &maps[0]);
+  int8conv_status st = activation_map_im2col(s, x, CBLK, pixels, count_w, count_h, &maps[0]);
   if (st != INT8CONV_OK) return st;
   st = filter_map_tiled(s, w, CBLK, b_rows, &maps[1]);
   if (st != INT8CONV_OK) return st;
@@ -659,8 +692,8 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
     st = output_map_tiled(y, g.M, g.K, &maps[2]);
     if (st != INT8CONV_OK) return st;
   }
-  const SmemPlan plan = smem_plan(CBLK, b_rows, STRIP ? g.a_rows : kBlockM, g.a_stages, g.stages);
-  auto kernel = conv_kernel<CBLK, STRIP, PAIR>;
+  const SmemPlan plan = smem_plan(CBLK, b_rows, SHIFT ? g.a_rows : kBlockM, g.a_stages, g.stages);
+  auto kernel = conv_kernel<CBLK, MODE, PAIR>;
   // At least half an SM's shared memory: one CTA per SM, so a CTA never waits
   // for another's TMEM columns.
   const uint32_t smem_bytes = plan.total > kOneCtaPerSm ? plan.total : kOneCtaPerSm;
@@ -698,17 +731,17 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   return err == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
 }
 
-template <bool STRIP, bool PAIR>
+template <int MODE, bool PAIR>
 static int8conv_status launch_cblk(const int8conv_shape &s, const ConvGeom &g, int cblk,
                                    const int8_t *x, const int8_t *w, const int32_t *b,
                                    int32_t *y, cudaStream_t stream) {
   switch (cblk) {
     case 128:
-      return launch_t<128, STRIP, PAIR>(s, g, x, w, b, y, stream);
+      return launch_t<128, MODE, PAIR>(s, g, x, w, b, y, stream);
     case 64:
-      return launch_t<64, STRIP, PAIR>(s, g, x, w, b, y, stream);
+      return launch_t<64, MODE, PAIR>(s, g, x, w, b, y, stream);
     default:
-      return launch_t<32, STRIP, PAIR>(s, g, x, w, b, y, stream);
+      return launch_t<32, MODE, PAIR>(s, g, x, w, b, y, stream);
   }
 }
 
@@ -716,37 +749,42 @@ static int8conv_status launch_cblk(const int8conv_shape &s, const ConvGeom &g, i
 // off when the filter tile is the full 256 columns and there are at least two
 // waves of 256-row tiles (5a: 357 vs 403 us, 5b: 92 vs 102 us); narrower or
 // smaller layers run faster as single CTAs (3b: 17 vs 23 us, 2: 17 vs 20 us).
-static bool use_pair(const int8conv_shape &s, bool strip) {
-  const int mode = pairing_mode();
-  if (mode == 1) return false;
+static bool use_pair(const int8conv_shape &s, int mode) {
+  const int pairing = pairing_mode();
+  if (pairing == 1) return false;
   ConvGeom g;
   int cblk = 0;
-  if (!plan_geometry(s, strip, true, g, cblk)) return false;
-  if (mode == 2) return true;
+  if (!plan_geometry(s, mode, true, g, cblk)) return false;
+  if (pairing == 2) return true;
   return g.bn == 256 && g.num_tiles >= device_info().sm_count;
 }
 
-template <bool STRIP>
-static int8conv_status launch_family(const int8conv_shape &s, const int8_t *x, const int8_t *w,
-                                     const int32_t *b, int32_t *y, cudaStream_t stream) {
+template <int MODE>
+static int8conv_status launch_mode(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                   const int32_t *b, int32_t *y, cudaStream_t stream) {
   ConvGeom g;
   int cblk = 0;
-  if (use_pair(s, STRIP)) {
-    if (!plan_geometry(s, STRIP, true, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
-    return launch_cblk<STRIP, true>(s, g, cblk, x, w, b, y, stream);
+  if (use_pair(s, MODE)) {
+    if (!plan_geometry(s, MODE, true, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+    return launch_cblk<MODE, true>(s, g, cblk, x, w, b, y, stream);
   }
-  if (!plan_geometry(s, STRIP, false, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
-  return launch_cblk<STRIP, false>(s, g, cblk, x, w, b, y, stream);
+  if (!plan_geometry(s, MODE, false, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+  return launch_cblk<MODE, false>(s, g, cblk, x, w, b, y, stream);
 }
 
 int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                     const int32_t *b, int32_t *y, cudaStream_t stream) {
-  return launch_family<false>(s, x, w, b, y, stream);
+  return launch_mode<kModeGeneric>(s, x, w, b, y, stream);
 }
 
 int8conv_status launch_strip_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                   const int32_t *b, int32_t *y, cudaStream_t stream) {
-  return launch_family<true>(s, x, w, b, y, stream);
+  return launch_mode<kModeStrip>(s, x, w, b, y, stream);
+}
+
+int8conv_status launch_halo_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                 const int32_t *b, int32_t *y, cudaStream_t stream) {
+  return launch_mode<kModeHalo>(s, x, w, b, y, stream);
 }
 
 }  // namespace i8c

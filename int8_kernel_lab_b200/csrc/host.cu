@@ -193,19 +193,19 @@ bool ensure_smem_attr(const void *kernel, int bytes) {
 }
 
 int8conv_status activation_map_im2col(const int8conv_shape &s, const int8_t *x, int channels,
-                                      int pixels, int count_w, CUtensorMap *map) {
-  const MapKey key = make_key(1, s, x, channels, pixels, count_w);
+                                      int pixels, int count_w, int count_h, CUtensorMap *map) {
+  MapKey key = make_key(1, s, x, channels, pixels, count_w);
+  key.pad = count_h;
   if (map_lookup(key, map)) return INT8CONV_OK;
   std::call_once(g_driver_once, load_driver_entry_points);
   if (!g_encode_im2col) return INT8CONV_CUDA_ERROR;
-  const int32_t out_h = (s.h + 2 * s.pad_h - s.dilation_h * (s.r - 1) - 1) / s.stride_h + 1;
   cuuint64_t dims[4] = {(cuuint64_t)s.c, (cuuint64_t)s.w, (cuuint64_t)s.h, (cuuint64_t)s.n};
   cuuint64_t strides[3] = {(cuuint64_t)s.c, (cuuint64_t)s.w * s.c, (cuuint64_t)s.h * s.w * s.c};
   // Bounding box per image: traversal starts at -pad and holds exactly
-  // count_w x out_h positions (stride apart); the upper corner is chosen so.
+  // count_w x count_h positions (stride apart); the upper corner is chosen so.
   int lower[2] = {-s.pad_w, -s.pad_h};
   int upper[2] = {-s.pad_w + (count_w - 1) * s.stride_w + 1 - s.w,
-                  -s.pad_h + (out_h - 1) * s.stride_h + 1 - s.h};
+                  -s.pad_h + (count_h - 1) * s.stride_h + 1 - s.h};
   cuuint32_t estr[4] = {1, (cuuint32_t)s.stride_w, (cuuint32_t)s.stride_h, 1};
   CUresult rc = g_encode_im2col(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t *>(x),
                                 dims, strides, lower, upper, (cuuint32_t)channels,

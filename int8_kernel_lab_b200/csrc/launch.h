@@ -38,10 +38,11 @@ bool ensure_smem_attr(const void *kernel, int bytes);
 
 // im2col tensor map over the NHWC activations: `channels` bytes per pixel
 // (swizzle = channels bytes), `pixels` traversal positions per load, and a
-// bounding box holding `count_w` positions per row (out_w for GENERIC,
-// out_w + s - 1 for STRIP) and out_h rows.
+// bounding box per image holding `count_w` positions per row (out_w for
+// GENERIC, the padded width for STRIP/HALO) and `count_h` rows (out_h, or the
+// padded height for HALO), starting at (-pad_w, -pad_h).
 int8conv_status activation_map_im2col(const int8conv_shape &s, const int8_t *x, int channels,
-                                      int pixels, int count_w, CUtensorMap *map);
+                                      int pixels, int count_w, int count_h, CUtensorMap *map);
 
 // Tiled tensor map over the KRSC filter viewed as [K][R*S][C], box
 // (channels, 1, rows).
@@ -57,6 +58,12 @@ int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, co
                                     const int32_t *b, int32_t *y, cudaStream_t stream);
 int8conv_status launch_strip_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                   const int32_t *b, int32_t *y, cudaStream_t stream);
+int8conv_status launch_host_pipeline(int strategy, const int8conv_shape &s, const int8_t *hx,
+                                     const int8_t *hw, const int32_t *hb, int32_t *hy,
+                                     int8_t *dx, int8_t *dw, int32_t *db, int32_t *dy,
+                                     int chunks, cudaStream_t stream);
+int8conv_status launch_halo_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                 const int32_t *b, int32_t *y, cudaStream_t stream);
 int8conv_status launch_splitk_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                    const int32_t *b, int32_t *y, cudaStream_t stream);
 

@@ -339,7 +339,7 @@ static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &
                                       const int8_t *x, const int8_t *w, const int32_t *b,
                                       int32_t *y, cudaStream_t stream) {
   CUtensorMap maps[2];
-  int8conv_status st = activation_map_im2col(s, x, CBLK, kBlockM, sg.g.Q, &maps[0]);
+  int8conv_status st = activation_map_im2col(s, x, CBLK, kBlockM, sg.g.Q, sg.g.P, &maps[0]);
   if (st != INT8CONV_OK) return st;
   st = filter_map_tiled(s, w, CBLK, sg.g.bn, &maps[1]);
   if (st != INT8CONV_OK) return st;

@@ -215,3 +215,25 @@ def test_device_wait_timeout_is_reported_and_context_survives(cuda, pairing):
     m.launch("generic", shape, dx, dw, db, dy)
     assert m.device_status() == _abi.OK
     assert np.array_equal(dy.cpu().numpy(), pyoracle.conv(shape, x, w, b))
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 64])
+def test_host_buffer_pipeline(cuda, chunks):
+    # int8conv_launch_host: pinned host buffers in, host output back, with the
+    # copies of image groups overlapped with the kernels.
+    torch = cuda
+    shape = m.load_workloads()["cfg2_mid_3x3"].with_batch(7)
+    x, w, b = m.make_inputs(shape, seed=3)
+    hx = torch.from_numpy(x).pin_memory()
+    hw = torch.from_numpy(w).pin_memory()
+    hb = torch.from_numpy(b).pin_memory()
+    hy = torch.full((shape.output_elements,), -1, dtype=torch.int32).pin_memory()
+    dx = torch.empty(shape.input_elements, dtype=torch.int8, device="cuda")
+    dw = torch.empty(shape.filter_elements, dtype=torch.int8, device="cuda")
+    db = torch.empty(shape.k, dtype=torch.int32, device="cuda")
+    dy = torch.empty(shape.output_elements, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    m.launch_host("auto", shape, hx, hw, hb, hy, dx, dw, db, dy, chunks=chunks, stream=s)
+    s.synchronize()
+    assert m.device_status() == _abi.OK
+    assert np.array_equal(hy.numpy(), pyoracle.conv(shape, x, w, b))

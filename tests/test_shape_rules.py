@@ -48,3 +48,28 @@ def test_ops_and_bytes_accounting():
     assert s.ops == 2 * 256 * 56 * 56 * 256 * 256 * 9
     assert s.compulsory_bytes == (256 * 56 * 56 * 256 + 256 * 9 * 256 + 4 * 256
                                   + 4 * 256 * 56 * 56 * 256)
+
+
+@pytest.mark.parametrize("name,expect", [
+    ("cfg4b_small_3x3", True), ("cfg4c_tail_k100", True), ("cfg2_mid_3x3", True),
+    ("cfg5b_dilated_3x3", True),    # dilation is a larger shift of the same tile
+    ("cfg3a_down_3x3_s2", False),   # stride 2
+    ("big_3x3_s1", False),          # 256-wide rows: the staged tile would exceed 512 pixels
+])
+def test_halo_predicate(name, expect):
+    assert m.load_workloads()[name].eligible("halo") is expect
+
+
+def test_splitk_needs_two_kblocks():
+    assert not m.ConvShape(1, 8, 8, 32, 8, 1, 1).eligible("splitk")     # one k-block
+    assert m.ConvShape(1, 8, 8, 256, 8, 1, 1).eligible("splitk")       # two 128-channel blocks
+    assert m.ConvShape(1, 8, 8, 32, 8, 3, 3, 1, 1).eligible("splitk")  # nine taps
+
+
+def test_dispatch_policy_on_baseline():
+    want = {"cfg4b_small_3x3": "splitk", "cfg4c_tail_k100": "splitk",
+            "cfg5a_stress_3x3": "generic", "cfg5b_dilated_3x3": "generic",
+            "cfg3b_pointwise": "generic"}
+    table = m.load_workloads()
+    for name, fam in want.items():
+        assert table[name].select() == fam, name
