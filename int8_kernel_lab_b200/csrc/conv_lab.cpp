@@ -15,7 +15,9 @@
 //     oracle_threads, graph_ms.
 // Validation compares EVERY output element (the reference checks 2048
 // strided samples above 65536 outputs, conv_lab.cu:72-77) against a direct
-// host convolution with the loop nest of conv_lab.cu:39-66.
+// host convolution with the loop nest of conv_lab.cu:39-66;
+// --validate-samples N checks the first and last output rows plus N random
+// outputs instead (for multi-Top stress shapes).
 // --strategy both = generic + strip (as in the reference); all = the four
 // families; auto = the dispatch policy's pick; or one family name.
 #include <cuda_runtime.h>
@@ -73,13 +75,14 @@ struct Options {
   double peak_tops = 4500.0;
   bool graph = true;
   int pairing = 0;
+  long long validate_samples = 0;  // 0: every output
 };
 
 [[noreturn]] void usage() {
   std::cerr << "usage: conv_lab [--strategy generic|strip|halo|splitk|both|all|auto] [--csv] "
                "[--warmup N] [--iterations N] [--case NAME] [--config CSV] "
                "[--values full|reference] [--seed S] [--batch N] [--peak-tops T] "
-               "[--no-graph] [--pairing auto|single|pair]\n";
+               "[--no-graph] [--pairing auto|single|pair] [--validate-samples N]\n";
   std::exit(EXIT_FAILURE);
 }
 
@@ -102,6 +105,7 @@ Options parse_options(int argc, char **argv) {
     else if (arg == "--seed") o.seed = static_cast<uint32_t>(std::stoul(value()));
     else if (arg == "--batch") o.batch = std::stoi(value());
     else if (arg == "--peak-tops") o.peak_tops = std::stod(value());
+    else if (arg == "--validate-samples") o.validate_samples = std::stoll(value());
     else if (arg == "--pairing") {
       const std::string v = value();
       o.pairing = v == "auto" ? 0 : v == "single" ? 1 : v == "pair" ? 2 : -1;
@@ -147,35 +151,73 @@ bool load_case(const std::string &path, const std::string &name, int8conv_shape 
   return false;
 }
 
-// Every output element against a direct host convolution: the loop nest of
-// the reference's reference_value (conv_lab.cu:39-66), all outputs, threaded.
+// Dot product of one tap over C channels, compiled for several x86 levels
+// (the loader picks the best one the host supports).
+__attribute__((target_clones("default", "arch=x86-64-v3", "arch=x86-64-v4"))) int32_t
+tap_dot(const int8_t *xp, const int8_t *wp, int c) {
+  int32_t sum = 0;
+  for (int i = 0; i < c; ++i) sum += int32_t(xp[i]) * int32_t(wp[i]);
+  return sum;
+}
+
+// One output element by direct convolution: the loop nest of the reference's
+// reference_value (conv_lab.cu:39-66).
+int32_t direct_value(const int8conv_shape &s, const int8conv_dims &d, const std::vector<int8_t> &x,
+                     const std::vector<int8_t> &w, const std::vector<int32_t> &b, int64_t m,
+                     int k) {
+  const int ox = static_cast<int>(m % d.out_w);
+  const int oy = static_cast<int>((m / d.out_w) % d.out_h);
+  const int64_t n = m / (static_cast<int64_t>(d.out_w) * d.out_h);
+  int32_t sum = b[k];
+  for (int fy = 0; fy < s.r; ++fy) {
+    const int iy = oy * s.stride_h + fy * s.dilation_h - s.pad_h;
+    if (iy < 0 || iy >= s.h) continue;
+    for (int fx = 0; fx < s.s; ++fx) {
+      const int ix = ox * s.stride_w + fx * s.dilation_w - s.pad_w;
+      if (ix < 0 || ix >= s.w) continue;
+      sum += tap_dot(&x[((n * s.h + iy) * s.w + ix) * s.c],
+                     &w[((static_cast<int64_t>(k) * s.r + fy) * s.s + fx) * s.c], s.c);
+    }
+  }
+  return sum;
+}
+
+// Compares the GPU output with direct convolution: every output when
+// `samples` is 0 (the default; the reference checks only 2048 strided samples
+// above 65536 outputs, conv_lab.cu:72-77), else the first and last output
+// rows plus `samples` seeded random outputs.
 bool validate_all(const int8conv_shape &s, const int8conv_dims &d,
                   const std::vector<int8_t> &x, const std::vector<int8_t> &w,
                   const std::vector<int32_t> &b, const std::vector<int32_t> &y,
-                  const char *label, int threads, double &ms) {
+                  const char *label, int threads, double &ms, long long samples = 0) {
   const auto t0 = std::chrono::steady_clock::now();
   std::vector<long long> first_bad(threads, -1);
   std::vector<std::thread> pool;
+  std::vector<int64_t> picks;
+  if (samples > 0) {
+    std::mt19937_64 rng(12345);
+    std::uniform_int_distribution<int64_t> pick(0, d.output_elements - 1);
+    for (int k = 0; k < s.k; ++k) {
+      picks.push_back(k);
+      picks.push_back((d.gemm_m - 1) * s.k + k);
+    }
+    for (long long i = 0; i < samples; ++i) picks.push_back(pick(rng));
+  }
   for (int t = 0; t < threads; ++t) {
     pool.emplace_back([&, t] {
-      for (int64_t m = t; m < d.gemm_m; m += threads) {
-        const int ox = static_cast<int>(m % d.out_w);
-        const int oy = static_cast<int>((m / d.out_w) % d.out_h);
-        const int64_t n = m / (static_cast<int64_t>(d.out_w) * d.out_h);
-        for (int k = 0; k < s.k; ++k) {
-          int32_t sum = b[k];
-          for (int fy = 0; fy < s.r; ++fy) {
-            const int iy = oy * s.stride_h + fy * s.dilation_h - s.pad_h;
-            if (iy < 0 || iy >= s.h) continue;
-            for (int fx = 0; fx < s.s; ++fx) {
-              const int ix = ox * s.stride_w + fx * s.dilation_w - s.pad_w;
-              if (ix < 0 || ix >= s.w) continue;
-              const int8_t *xp = &x[((n * s.h + iy) * s.w + ix) * s.c];
-              const int8_t *wp = &w[((static_cast<int64_t>(k) * s.r + fy) * s.s + fx) * s.c];
-              for (int c = 0; c < s.c; ++c) sum += int32_t(xp[c]) * int32_t(wp[c]);
-            }
+      if (samples > 0) {
+        for (size_t i = t; i < picks.size(); i += threads) {
+          const int64_t idx = picks[i];
+          if (y[idx] != direct_value(s, d, x, w, b, idx / s.k, static_cast<int>(idx % s.k))) {
+            first_bad[t] = idx;
+            return;
           }
-          if (y[m * s.k + k] != sum) {
+        }
+        return;
+      }
+      for (int64_t m = t; m < d.gemm_m; m += threads) {
+        for (int k = 0; k < s.k; ++k) {
+          if (y[m * s.k + k] != direct_value(s, d, x, w, b, m, k)) {
             first_bad[t] = m * s.k + k;
             return;
           }
@@ -262,7 +304,13 @@ std::string fmt(double v) {
 }  // namespace
 
 int main(int argc, char **argv) {
-  const Options options = parse_options(argc, argv);
+  Options parsed;
+  try {
+    parsed = parse_options(argc, argv);
+  } catch (const std::exception &) {  // a non-numeric value for a numeric flag
+    usage();
+  }
+  const Options options = parsed;
   int8conv_set_cta_pairing(options.pairing);
   const std::string config = options.config.empty() ? default_config(argv[0]) : options.config;
   int8conv_shape shape;
@@ -349,7 +397,7 @@ int main(int argc, char **argv) {
           "copy output");
     double vms = 0;
     correct[f] = validate_all(shape, d, input, filter, bias, output,
-                              int8conv_strategy_name(f), threads, vms);
+                              int8conv_strategy_name(f), threads, vms, options.validate_samples);
     oracle_ms = std::max(oracle_ms, vms);
     if (!correct[f]) continue;
     ms[f] = measure(launch, options.warmup, options.iterations);

@@ -31,6 +31,8 @@ def main(argv=None) -> int:
     ap.add_argument("--strategy", default="all")
     ap.add_argument("--values", default="full", choices=("full", "reference"))
     ap.add_argument("--pairing", default="auto", choices=("auto", "single", "pair"))
+    ap.add_argument("--full-validate-ops", type=float, default=2e11,
+                    help="shapes with more ops validate 200000 sampled outputs, not all")
     ap.add_argument("--conv-lab", default=str(PKG / "lib" / "conv_lab"))
     args = ap.parse_args(argv)
     with open(args.configs, newline="") as stream:
@@ -42,11 +44,19 @@ def main(argv=None) -> int:
     args.output.parent.mkdir(parents=True, exist_ok=True)
     measurements = []
     status = 0
+    shapes = {r["name"]: r for r in rows}
     for case in requested:
+        r = shapes[case]
+        oh = int((int(r["h"]) + 2 * int(r["pad_h"]) - int(r["dilation_h"]) * (int(r["r"]) - 1) - 1)
+                 / int(r["stride_h"])) + 1
+        ow = int((int(r["w"]) + 2 * int(r["pad_w"]) - int(r["dilation_w"]) * (int(r["s"]) - 1) - 1)
+                 / int(r["stride_w"])) + 1
+        ops = 2.0 * int(r["n"]) * oh * ow * int(r["k"]) * int(r["c"]) * int(r["r"]) * int(r["s"])
+        extra = ["--validate-samples", "200000"] if ops > args.full_validate_ops else []
         result = subprocess.run(
             [args.conv_lab, "--case", case, "--config", str(args.configs), "--strategy",
              args.strategy, "--iterations", str(args.iterations), "--warmup", str(args.warmup),
-             "--values", args.values, "--pairing", args.pairing, "--csv"],
+             "--values", args.values, "--pairing", args.pairing, "--csv"] + extra,
             text=True, capture_output=True)
         if result.returncode != 0:
             status = 1
