@@ -61,7 +61,7 @@ struct SplitSwizzle<32> {
 };
 
 template <int CBLK>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kSplitThreads, 1)
     splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
                   const __grid_constant__ CUtensorMap tmap_w, const SplitGeom sg,
                   const int32_t *__restrict__ bias, int32_t *__restrict__ out,
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int groups = g.bn / 4;  // 16-byte column groups per row
   const uint32_t part_base = smem_u32(partial);
   const bool vec_k = (g.K & 3) == 0;
-  for (int item = threadIdx.x; item < (r_end - r_begin) * groups; item += kThreads) {
+  for (int item = threadIdx.x; item < (r_end - r_begin) * groups; item += kSplitThreads) {
     const int rr = r_begin + item / groups;
     const int cg = item - (item / groups) * groups;
     const int m = m0 + rr;
@@ -355,7 +355,7 @@ static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sg.g.num_tiles * sg.splits, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kSplitThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
