@@ -109,7 +109,7 @@ class ClockSampler:
             self.out = tempfile.TemporaryFile(mode="w+")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-i", gpu_id, "-lms", "100"], stdout=self.out, stderr=subprocess.DEVNULL)
+                 "-i", gpu_id, "-lms", "20"], stdout=self.out, stderr=subprocess.DEVNULL)
 
     def stop(self):
         if self.proc is None:

@@ -207,6 +207,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialisation: the set-up above may run
+  // while the previous kernel in the stream finishes; no thread reads or
+  // writes global memory before that kernel is complete.
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -706,27 +711,23 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
     slot.store(kMaxSmem, std::memory_order_relaxed);
   }
   const RunCtl ctl = run_ctl();
-  cudaError_t err;
-  if constexpr (PAIR) {
-    const int pairs = g.num_tiles < dev.sm_count / 2 ? g.num_tiles : dev.sm_count / 2;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem_bytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], g, b, y, ctl);
-  } else {
-    const int grid = g.num_tiles < dev.sm_count ? g.num_tiles : dev.sm_count;
-    kernel<<<grid, kThreads, smem_bytes, stream>>>(maps[0], maps[1], maps[2], g, b, y, ctl);
-    err = cudaGetLastError();
-  }
+  const int ctas = PAIR ? 2 * (g.num_tiles < dev.sm_count / 2 ? g.num_tiles : dev.sm_count / 2)
+                        : (g.num_tiles < dev.sm_count ? g.num_tiles : dev.sm_count);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = PAIR ? 2 : 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], g, b, y, ctl);
   note_launch();
   return err == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
 }

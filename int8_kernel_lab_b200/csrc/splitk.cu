@@ -111,6 +111,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   bool epi_ok = true;
+  // Programmatic stream serialisation: nothing touches global memory before
+  // the previous kernel in the stream is complete.
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -358,13 +362,15 @@ static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &
   cfg.blockDim = dim3(kSplitThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = sg.splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], sg, b, y, run_ctl());
   note_launch();
   return err == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
