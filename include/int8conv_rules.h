@@ -88,9 +88,26 @@ I8C_RULE int i8c_strip_eligible(const int8conv_shape *s) {
          i8c_corner_ok(i8c_upper_corner(s->w, s->pad_w, 1, i8c_out_w(s) + s->s - 1));
 }
 
-/* Channel block (bytes of C per k-block) the kernels use for a shape. */
+/* Channel block (bytes of C per k-block, one swizzle width: 128, 64 or 32)
+ * the kernels use for a shape.  Each k-block costs its CBLK bytes of MMA work
+ * plus a fixed pipeline round trip worth about 64 bytes; channels past C in
+ * the last block are zero-filled by TMA.  The cheapest block wins, ties going
+ * to the one with less zero padding (C = 48 -> 64, C = 96 -> 128,
+ * C = 192 -> 64, C % 128 == 0 -> 128). */
 I8C_RULE int32_t i8c_channel_block(int32_t c) {
-  return c % 128 == 0 ? 128 : c % 64 == 0 ? 64 : 32;
+  int32_t best = 32;
+  int64_t best_cost = -1, best_pad = 0;
+  for (int32_t cb = 128; cb >= 32; cb /= 2) {
+    const int64_t blocks = (c + cb - 1) / cb;
+    const int64_t cost = blocks * (cb + 64);
+    const int64_t pad = blocks * cb - c;
+    if (best_cost < 0 || cost < best_cost || (cost == best_cost && pad < best_pad)) {
+      best = cb;
+      best_cost = cost;
+      best_pad = pad;
+    }
+  }
+  return best;
 }
 
 /* SPLITK: the R*S*C reduction of each output tile is split across the CTAs

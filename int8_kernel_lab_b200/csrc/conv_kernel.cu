@@ -50,6 +50,7 @@
 #include <atomic>
 
 #include "conv_common.h"
+#include "int8conv_rules.h"
 #include "launch.h"
 #include "sm100.cuh"
 
@@ -578,11 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Host side
 // ---------------------------------------------------------------------------
 
-static int pick_cblk(int c) {
-  if (c % 128 == 0) return 128;
-  if (c % 64 == 0) return 64;
-  return 32;
-}
+static int pick_cblk(int c) { return i8c_channel_block(c); }
 
 static int pick_bn(int k) {
   if (k <= 256) return (k + 15) / 16 * 16;

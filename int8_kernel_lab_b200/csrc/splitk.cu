@@ -22,6 +22,7 @@
 #include <atomic>
 
 #include "conv_common.h"
+#include "int8conv_rules.h"
 #include "launch.h"
 #include "sm100.cuh"
 
@@ -273,11 +274,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 // Host side
 // ---------------------------------------------------------------------------
 
-static int split_cblk(int c) {
-  if (c % 128 == 0) return 128;
-  if (c % 64 == 0) return 64;
-  return 32;
-}
+static int split_cblk(int c) { return i8c_channel_block(c); }
 
 // Plans a split-K launch; false if the shape has too little reduction to split.
 static bool plan_split(const int8conv_shape &s, int sm_count, SplitGeom &sg, int &cblk) {
