@@ -134,6 +134,48 @@ int8conv_status int8conv_launch_splitk(const int8conv_shape *shape,
                                        void *workspace, size_t workspace_bytes,
                                        void *stream);
 
+/* ---- requantised int8 output ---------------------------------------------------*/
+
+/* Output layouts of the requantised launch. */
+typedef enum int8conv_layout {
+  INT8CONV_LAYOUT_NHWC = 0,        /* int8 [N][out_h][out_w][K]: the next layer's input layout */
+  INT8CONV_LAYOUT_NCHW_VECT_C = 1  /* cuDNN INT8x32: int8 [N][K/32][out_h][out_w][32], K % 32 == 0 */
+} int8conv_layout;
+
+/* Per-output-channel fixed-point scaling (gemmlowp / TensorFlow Lite
+ * "quantized multiplier").  With t = output[m*K + k] of the int32 contract
+ * (accumulator + bias, two's-complement):
+ *   e = clamp(exponent[k], -31, 31)
+ *   t = e > 0 ? saturate_int32(t * 2^e) : t
+ *   u = (t * multiplier[k] + nudge) / 2^31    truncating division; nudge = 2^30 for
+ *                                             t * multiplier >= 0, else 1 - 2^30;
+ *                                             INT32_MIN * INT32_MIN gives INT32_MAX
+ *   v = e < 0 ? u / 2^-e rounded half away from zero : u
+ *   y = clamp(v + zero_point, relu ? zero_point : -128, 127)
+ * multiplier = 2^30, exponent = 1 gives y = clamp(t, -128, 127), the int8
+ * output of cuDNN's INT8x32 convolution with alpha = 1, beta = 0 (the
+ * reference's cuDNN comparison, include/cudnn_legacy.cuh:51-55). */
+typedef struct int8conv_requant {
+  const int32_t *multiplier; /* K entries, device memory, 16-byte aligned */
+  const int32_t *exponent;   /* K entries, device memory, 16-byte aligned */
+  int32_t zero_point;        /* in [-128, 127] */
+  int32_t relu;              /* 0 or 1: fused ReLU (clamp below at zero_point) */
+  int32_t layout;            /* int8conv_layout */
+} int8conv_requant;
+
+/* Launch one family (or INT8CONV_AUTO) with the int8 epilogue above instead
+ * of the int32 output: `output` receives N*out_h*out_w*K int8 values in
+ * `requant->layout`.  No reference counterpart (the reference writes int32
+ * only; its cuDNN baseline writes INT8x32).  NOT_ELIGIBLE for
+ * INT8CONV_LAYOUT_NCHW_VECT_C when K % 32 != 0; BAD_ARGUMENT for a zero point,
+ * relu flag or layout out of range; BAD_POINTER for a NULL or misaligned
+ * multiplier / exponent array. */
+int8conv_status int8conv_launch_requant(int strategy, const int8conv_shape *shape,
+                                        const int8_t *input, const int8_t *filter,
+                                        const int32_t *bias, const int8conv_requant *requant,
+                                        int8_t *output, void *workspace,
+                                        size_t workspace_bytes, void *stream);
+
 /* ---- host buffers ------------------------------------------------------------*/
 
 /* End-to-end convolution of HOST buffers (no reference counterpart; the

@@ -118,6 +118,28 @@ I8C_RULE int i8c_splitk_eligible(const int8conv_shape *s) {
          (int64_t)s->r * s->s * ((s->c + i8c_channel_block(s->c) - 1) / i8c_channel_block(s->c)) >= 2;
 }
 
+/* Thread-block clusters that can be resident at once on a B200 (148 SMs), by
+ * cluster size 0..8, with one CTA per SM (every kernel here asks for at least
+ * half an SM's shared memory).  Measured with cudaOccupancyMaxActiveClusters;
+ * GPC boundaries make the larger sizes lose SMs (8 x 15 = 120 of 148). */
+#define I8C_B200_CLUSTERS {0, 148, 74, 45, 33, 26, 22, 15, 15}
+
+/* SPLITK cluster size for `tiles` output tiles and `kblocks` k-blocks: the
+ * largest split in [2, min(8, kblocks)] whose clusters all fit in one wave
+ * (tiles <= clusters[split]); 0 if none does.  `clusters` is indexed by
+ * cluster size, like I8C_B200_CLUSTERS. */
+I8C_RULE int32_t i8c_split_count(int64_t tiles, int64_t kblocks, const int32_t *clusters) {
+  for (int32_t split = kblocks < 8 ? (int32_t)kblocks : 8; split >= 2; --split)
+    if (tiles <= clusters[split]) return split;
+  return 0;
+}
+
+/* Output tiles of the SPLITK kernel: 128 rows x BN columns, BN <= 128. */
+I8C_RULE int64_t i8c_split_tiles(const int8conv_shape *s) {
+  const int64_t m = (int64_t)s->n * i8c_out_h(s) * i8c_out_w(s);
+  return (m + 127) / 128 * ((s->k + 127) / 128);
+}
+
 /* HALO: positions run over the zero-padded image (Hp x Wp, Hp = out_h +
  * (R-1)*dh, Wp = out_w + (S-1)*dw); one staged halo tile of
  * 128 + (R-1)*dh*Wp + (S-1)*dw pixels per channel block feeds all R*S taps.

@@ -8,14 +8,15 @@ per-family eligibility predicates.  All compute runs in libint8conv.so
 from ._abi import (AUTO, GENERIC, HALO, SPLITK, STRIP, STRATEGIES, Int8ConvError,  # noqa: F401
                    LIB_PATH)
 from .api import (conv2d, debug_starve_producer, device_status, launch,  # noqa: F401
-                  launch_count, launch_host, launch_generic, launch_generic_sm80, launch_spatial_strip,
+                  launch_count, launch_host, launch_generic, launch_generic_sm80, launch_requant,
+                  launch_spatial_strip,
                   set_cta_pairing, set_wait_limit_ns, spatial_strip_eligible, workspace_bytes)
 from .data import REFERENCE_SEED, make_inputs  # noqa: F401
 from .shape import (BASELINE_CASES, ConvShape, baseline_shapes, load_workloads)  # noqa: F401
 
 __all__ = [
     "ConvShape", "load_workloads", "baseline_shapes", "BASELINE_CASES", "make_inputs",
-    "launch", "launch_host", "launch_generic", "launch_generic_sm80", "launch_spatial_strip",
+    "launch", "launch_host", "launch_requant", "launch_generic", "launch_generic_sm80", "launch_spatial_strip",
     "spatial_strip_eligible", "conv2d", "workspace_bytes", "device_status", "launch_count",
     "Int8ConvError", "STRATEGIES",
 ]

@@ -36,6 +36,18 @@ AUTO = 100
 STRATEGIES = {"generic": GENERIC, "strip": STRIP, "halo": HALO, "splitk": SPLITK, "auto": AUTO}
 
 
+# int8conv_layout
+LAYOUT_NHWC = 0
+LAYOUT_NCHW_VECT_C = 1
+LAYOUTS = {"nhwc": LAYOUT_NHWC, "nchw_vect_c": LAYOUT_NCHW_VECT_C}
+
+
+class CRequant(ctypes.Structure):
+    _fields_ = [("multiplier", ctypes.c_void_p), ("exponent", ctypes.c_void_p),
+                ("zero_point", ctypes.c_int32), ("relu", ctypes.c_int32),
+                ("layout", ctypes.c_int32)]
+
+
 class CShape(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in SHAPE_FIELDS]
 
@@ -67,6 +79,9 @@ SIGNATURES = {
     "int8conv_launch_halo": (ctypes.c_int, [_SP, _P, _P, _P, _P, _P]),
     "int8conv_launch_splitk": (ctypes.c_int, [_SP, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     "int8conv_launch_host": (ctypes.c_int, [ctypes.c_int, _SP] + [_P] * 8 + [ctypes.c_int, _P]),
+    "int8conv_launch_requant": (ctypes.c_int, [ctypes.c_int, _SP, _P, _P, _P,
+                                               ctypes.POINTER(CRequant), _P, _P, ctypes.c_size_t,
+                                               _P]),
     "int8conv_device_status": (ctypes.c_int, []),
     "int8conv_set_wait_limit_ns": (None, [ctypes.c_uint64]),
     "int8conv_debug_starve_producer": (None, [ctypes.c_int]),

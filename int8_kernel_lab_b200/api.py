@@ -48,7 +48,7 @@ def _check_tensors(shape: ConvShape, x, w, b, y) -> None:
         ("bias", b, torch.int32, shape.k),
         ("output", y, torch.int32, shape.output_elements),
     ):
-        if isinstance(t, int):
+        if t is None or isinstance(t, int):
             continue
         if not t.is_cuda or t.dtype != dtype or not t.is_contiguous() or t.numel() != count:
             raise ValueError(
@@ -130,6 +130,35 @@ def launch_host(strategy: str, shape: ConvShape, hx, hw, hb, hy, dx, dw, db, dy,
         _abi.STRATEGIES[strategy], shape.c_struct(), _ptr(hx), _ptr(hw), _ptr(hb), _ptr(hy),
         _ptr(dx), _ptr(dw), _ptr(db), _ptr(dy), int(chunks), _stream(stream))
     _abi.check(status, f"{strategy} host launch of {shape}")
+
+
+def launch_requant(strategy: str, shape: ConvShape, x, w, b, multiplier, exponent, y, *,
+                   zero_point: int = 0, relu: bool = False, layout: str = "nhwc",
+                   workspace=None, workspace_bytes: int = 0, stream=None) -> None:
+    """int8conv_launch_requant: the convolution with an int8 epilogue.
+
+    `multiplier` and `exponent` are K-entry int32 CUDA tensors (Q31 multiplier
+    and power-of-two exponent per output channel); `y` is an int8 CUDA tensor
+    of N*out_h*out_w*K elements in `layout` ('nhwc' or 'nchw_vect_c', cuDNN's
+    INT8x32).  No reference counterpart: the reference's kernels write int32."""
+    import torch
+
+    _check_tensors(shape, x, w, b, None)
+    for name, t, dtype, count in (("multiplier", multiplier, torch.int32, shape.k),
+                                  ("exponent", exponent, torch.int32, shape.k),
+                                  ("output", y, torch.int8, shape.output_elements)):
+        if isinstance(t, int):
+            continue
+        if not t.is_cuda or t.dtype != dtype or not t.is_contiguous() or t.numel() != count:
+            raise ValueError(
+                f"{name}: expected a contiguous CUDA {dtype} tensor of {count} elements, "
+                f"got {t.dtype} {tuple(t.shape)} on {t.device}")
+    rq = _abi.CRequant(_ptr(multiplier), _ptr(exponent), int(zero_point), 1 if relu else 0,
+                       _abi.LAYOUTS[layout])
+    status = _abi.lib.int8conv_launch_requant(
+        _abi.STRATEGIES[strategy], shape.c_struct(), _ptr(x), _ptr(w), _ptr(b), rq, _ptr(y),
+        _ptr(workspace), int(workspace_bytes), _stream(stream))
+    _abi.check(status, f"{strategy} requantised launch of {shape}")
 
 
 def device_status() -> int:

@@ -87,6 +87,8 @@ int int8conv_select(const int8conv_shape *shape) {
   //    (5a 357 vs 396 us, 5c 39 vs 51 us).
   //  * SPLITK when the layer has too few 128-row output tiles to occupy half
   //    the GPU but a reduction deep enough to split (7x7 and 14x14 layers).
+  //    The split must fit in one wave of resident clusters (B200 table):
+  //    two waves lost to GENERIC in the sweep (batch8_3x3, darknet_down_52).
   if (!i8c_shape_valid(shape)) return INT8CONV_GENERIC;
   const int64_t m = static_cast<int64_t>(shape->n) * i8c_out_h(shape) * i8c_out_w(shape);
   const int64_t n_tiles = (shape->k + 255) / 256;
@@ -94,7 +96,9 @@ int int8conv_select(const int8conv_shape *shape) {
   const int32_t cblk = i8c_channel_block(shape->c);
   const int64_t kblocks =
       static_cast<int64_t>(shape->r) * shape->s * ((shape->c + cblk - 1) / cblk);
-  if (int8conv_eligible(shape, INT8CONV_SPLITK) && tiles < 74 && kblocks >= 8)
+  const int32_t clusters[9] = I8C_B200_CLUSTERS;
+  if (int8conv_eligible(shape, INT8CONV_SPLITK) && tiles < 74 && kblocks >= 8 &&
+      i8c_split_count(i8c_split_tiles(shape), kblocks, clusters) >= 2)
     return INT8CONV_SPLITK;
   return INT8CONV_GENERIC;
 }
@@ -178,6 +182,38 @@ int8conv_status int8conv_launch_splitk(const int8conv_shape *shape, const int8_t
                                        void *stream) {
   return launch_family(INT8CONV_SPLITK, shape, input, filter, bias, output, workspace,
                        workspace_bytes, stream);
+}
+
+int8conv_status int8conv_launch_requant(int strategy, const int8conv_shape *shape,
+                                        const int8_t *input, const int8_t *filter,
+                                        const int32_t *bias, const int8conv_requant *requant,
+                                        int8_t *output, void *workspace, size_t workspace_bytes,
+                                        void *stream) {
+  if (!i8c_shape_valid(shape)) return INT8CONV_BAD_SHAPE;
+  if (requant == nullptr) return INT8CONV_BAD_ARGUMENT;
+  if (requant->layout != INT8CONV_LAYOUT_NHWC && requant->layout != INT8CONV_LAYOUT_NCHW_VECT_C)
+    return INT8CONV_BAD_ARGUMENT;
+  if (requant->zero_point < -128 || requant->zero_point > 127) return INT8CONV_BAD_ARGUMENT;
+  if (requant->relu != 0 && requant->relu != 1) return INT8CONV_BAD_ARGUMENT;
+  if (strategy == INT8CONV_AUTO) strategy = int8conv_select(shape);
+  if (strategy < 0 || strategy >= INT8CONV_NUM_STRATEGIES) return INT8CONV_BAD_ARGUMENT;
+  if (!int8conv_eligible(shape, strategy)) return INT8CONV_NOT_ELIGIBLE;
+  if (requant->layout == INT8CONV_LAYOUT_NCHW_VECT_C && shape->k % 32 != 0)
+    return INT8CONV_NOT_ELIGIBLE;
+  if (!aligned16(input) || !aligned16(filter) || !aligned16(bias) || !aligned16(output) ||
+      !aligned16(requant->multiplier) || !aligned16(requant->exponent))
+    return INT8CONV_BAD_POINTER;
+  if (workspace_bytes < int8conv_workspace_bytes(shape, strategy))
+    return INT8CONV_WORKSPACE_TOO_SMALL;
+  (void)workspace;
+  const int8conv_status dev = i8c::check_device();
+  if (dev != INT8CONV_OK) return dev;
+  const i8c::Requant rq{requant->multiplier, requant->exponent, requant->zero_point,
+                        requant->relu, requant->layout};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (strategy == INT8CONV_SPLITK)
+    return i8c::launch_splitk_requant(*shape, input, filter, bias, rq, output, st);
+  return i8c::launch_conv_requant(strategy, *shape, input, filter, bias, rq, output, st);
 }
 
 int8conv_status int8conv_launch_host(int strategy, const int8conv_shape *shape,

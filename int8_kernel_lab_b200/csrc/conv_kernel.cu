@@ -133,12 +133,66 @@ __device__ __forceinline__ void commit_to(uint64_t *bar) {
     umma_commit(bar);
 }
 
-template <int CBLK, int MODE, bool PAIR>
-__global__ void __launch_bounds__(kThreads, 1)
+// Bias plus requantisation of one thread's 32 accumulators (columns col0..,
+// this warp's row): four channels per word.  Columns at or past the tile
+// width or K get zero parameters; they are never stored.  `lo` is the lower
+// clamp (the zero point with ReLU, else -128).
+__device__ __forceinline__ void requant_block(const uint32_t (&v)[32], const int32_t *bias,
+                                              const Requant &rq, int col0, int cols_left,
+                                              int K, int32_t lo, uint32_t (&w8)[8]) {
+  const bool vec4 = (K & 3) == 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = col0 + 4 * j;
+    int32_t bb[4], mm[4], ee[4];
+    if (vec4) {
+      const bool in = 4 * j < cols_left && c < K;
+      const int4 b4 = in ? __ldg(reinterpret_cast<const int4 *>(bias + c)) : make_int4(0, 0, 0, 0);
+      const int4 m4 =
+          in ? __ldg(reinterpret_cast<const int4 *>(rq.multiplier + c)) : make_int4(0, 0, 0, 0);
+      const int4 e4 =
+          in ? __ldg(reinterpret_cast<const int4 *>(rq.exponent + c)) : make_int4(0, 0, 0, 0);
+      bb[0] = b4.x, bb[1] = b4.y, bb[2] = b4.z, bb[3] = b4.w;
+      mm[0] = m4.x, mm[1] = m4.y, mm[2] = m4.z, mm[3] = m4.w;
+      ee[0] = e4.x, ee[1] = e4.y, ee[2] = e4.z, ee[3] = e4.w;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const bool in = 4 * j + t < cols_left && c + t < K;
+        bb[t] = in ? __ldg(bias + c + t) : 0;
+        mm[t] = in ? __ldg(rq.multiplier + c + t) : 0;
+        ee[t] = in ? __ldg(rq.exponent + c + t) : 0;
+      }
+    }
+    int32_t y[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      y[t] = rq_apply_dev(static_cast<int32_t>(v[4 * j + t] + static_cast<uint32_t>(bb[t])),
+                          rq_channel(mm[t], ee[t]), rq.zero_point, lo);
+    w8[j] = rq_pack4(y[0], y[1], y[2], y[3]);
+  }
+}
+
+// Epilogue warps: 4 for int32 output (one per TMEM lane quarter); 16 for the
+// requantised int8 output, whose per-element fixed-point arithmetic needs the
+// issue slots (four warps per lane quarter, each owning every fourth
+// 32-column block).
+template <bool REQ>
+constexpr int epilogue_warps() {
+  return REQ ? 16 : 4;
+}
+template <bool REQ>
+constexpr int kernel_threads() {
+  return 64 + 32 * epilogue_warps<REQ>();
+}
+
+template <int CBLK, int MODE, bool PAIR, bool REQ>
+__global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
     conv_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_w,
                 const __grid_constant__ CUtensorMap tmap_y, const ConvGeom g,
-                const int32_t *__restrict__ bias, int32_t *__restrict__ out, const RunCtl ctl) {
+                const int32_t *__restrict__ bias, int32_t *__restrict__ out, const RunCtl ctl,
+                const Requant rq) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment: the SW128 atom (8 rows x 128 B) starts on it.  The
   // offset is the same in both CTAs of a pair (same kernel, same smem size).
@@ -186,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       // One arrival per epilogue warp (of both CTAs for a pair).
-      mbar_init(&tempty[i], PAIR ? 8 : 4);
+      mbar_init(&tempty[i], (PAIR ? 2 : 1) * epilogue_warps<REQ>());
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -425,6 +479,117 @@ __global__ void __launch_bounds__(kThreads, 1)
       // are done; the leader's final commit arrives here too.
       mbar_wait(drain, 0, wctx, kStatusTimeoutTeardown);
     }
+  } else if constexpr (REQ) {
+    // ---------------- int8 epilogue (warps 2..17) ----------------
+    constexpr int kGroups = epilogue_warps<REQ>() / 4;
+    const int quarter = warp & 3;          // TMEM lane quarter this warp may access
+    const int cgroup = (warp - 2) >> 2;    // 32-column blocks cgroup, cgroup + 4, ...
+    const int row = quarter * 32 + lane;
+    const int m_limit = SHIFT ? g.Mp : g.M;
+    const uint32_t tempty_leader0 =
+        PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
+    const uint32_t tempty_leader1 =
+        PAIR ? mapa_shared(smem_u32(&tempty[1]), 0) : smem_u32(&tempty[1]);
+    const int32_t lo = rq.relu ? rq.zero_point : -128;
+    int8_t *out8 = reinterpret_cast<int8_t *>(out);
+    // Two 32-row x 32-byte staging buffers per warp (TMA store source).
+    uint8_t *stg_w = reinterpret_cast<uint8_t *>(staging) + (warp - 2) * 2048;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int ci = 0;
+    for (int tile = tile_first; tile < g.num_tiles; tile += tile_step) {
+      const int m_tile = tile / g.n_tiles;
+      const int n_tile = tile - m_tile * g.n_tiles;
+      const int pos = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + row;
+      const int n0 = n_tile * g.bn;
+      bool valid = pos < m_limit;
+      int m = pos;
+      if constexpr (SHIFT) {
+        const int img = pos / g.PWp;
+        const int rem = pos - img * g.PWp;
+        const int i = rem / g.Wp;
+        const int j = rem - i * g.Wp;
+        valid = valid && j < g.Q && i < g.P;
+        m = (img * g.P + i) * g.Q + j;
+      }
+      // Every warp, with or without a block of this tile, waits for the
+      // accumulator, so all of them arrive on tempty once per tile.
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, wctx, kStatusTimeoutAccum)))
+        break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * g.acc_stride;
+      const int row0 = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + quarter * 32;
+      bool released = false;
+      auto release = [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR)
+            mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+          else
+            mbar_arrive(&tempty[acc]);
+        }
+        released = true;
+      };
+      for (int c0 = 32 * cgroup; c0 < g.bn; c0 += 32 * kGroups) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + c0, v);
+        tmem_ld_wait();
+        if (c0 + 32 * kGroups >= g.bn) release();  // this warp's last read of the tile
+        const int col0 = n0 + c0;
+        uint32_t w8[8];
+        requant_block(v, bias, rq, col0, g.bn - c0, g.K, lo, w8);
+        const int4 lo16 = make_int4(static_cast<int32_t>(w8[0]), static_cast<int32_t>(w8[1]),
+                                    static_cast<int32_t>(w8[2]), static_cast<int32_t>(w8[3]));
+        const int4 hi16 = make_int4(static_cast<int32_t>(w8[4]), static_cast<int32_t>(w8[5]),
+                                    static_cast<int32_t>(w8[6]), static_cast<int32_t>(w8[7]));
+        if (g.tma_store) {
+          // 32 rows x 32 bytes leave as one TMA store (columns >= K, rows >= M
+          // clipped); the buffer was read by the store two blocks ago.
+          int4 *stg = reinterpret_cast<int4 *>(stg_w + (ci & 1) * 1024);
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          stg[2 * lane] = lo16;
+          stg[2 * lane + 1] = hi16;
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_y, stg, col0, row0);
+            bulk_commit_group();
+          }
+          ++ci;
+        } else if (valid && col0 < g.K) {
+          if (rq.layout == 1) {
+            // NCHW_VECT_C: the block is one 32-channel vector of this pixel
+            // (bn, K and col0 are multiples of 32); a warp writes 1 KB.
+            const int img = m / g.PQ;
+            const int pq = m - img * g.PQ;
+            int4 *dst = reinterpret_cast<int4 *>(
+                out8 + ((static_cast<int64_t>(img) * (g.K >> 5) + (col0 >> 5)) * g.PQ + pq) * 32);
+            __stcs(dst, lo16);
+            __stcs(dst + 1, hi16);
+          } else {
+            int8_t *dst = out8 + static_cast<int64_t>(m) * g.K + col0;
+            const int span = g.bn - c0 < g.K - col0 ? g.bn - c0 : g.K - col0;
+            if (span >= 32 && (g.K & 15) == 0) {
+              __stcs(reinterpret_cast<int4 *>(dst), lo16);
+              __stcs(reinterpret_cast<int4 *>(dst) + 1, hi16);
+            } else {
+#pragma unroll
+              for (int t = 0; t < 32; ++t)
+                if (t < span) dst[t] = static_cast<int8_t>((w8[t >> 2] >> (8 * (t & 3))) & 0xffu);
+            }
+          }
+        }
+      }
+      if (!released) release();  // no block of this tile for this warp
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (g.tma_store && lane == 0) bulk_wait_group_all();
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
@@ -473,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q = lane & 7;    // 16-byte column group this lane stores
       const int rsub = lane >> 3;
       const int row0 = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + quarter * 32;
-      for (int c0 = 0; c0 < g.bn; c0 += 32, ++ci) {
+      for (int c0 = 0; c0 < g.bn; c0 += 32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + c0, v);
         tmem_ld_wait();
@@ -509,6 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_store_2d(&tmap_y, stg, col0, row0);
             bulk_commit_group();
           }
+          ++ci;
           continue;
         }
         int4 *stg = stg_w;
@@ -581,13 +747,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 static int pick_cblk(int c) { return i8c_channel_block(c); }
 
-static int pick_bn(int k) {
-  if (k <= 256) return (k + 15) / 16 * 16;
-  // Balance the N tiles: the smallest multiple of 16 giving ceil(k/256) tiles.
+// `align` = 16, or 32 when every 32-column block must hold whole
+// 32-channel vectors (NCHW_VECT_C output).
+static int pick_bn(int k, int align) {
+  if (k <= 256) return (k + align - 1) / align * align;
+  // Balance the N tiles: the smallest multiple of `align` giving ceil(k/256) tiles.
   const int tiles = (k + 255) / 256;
   const int per = (k + tiles - 1) / tiles;
-  return (per + 15) / 16 * 16;
+  return (per + align - 1) / align * align;
 }
+
+// Output of a launch: the int32 contract or one of the int8 layouts.
+constexpr int kOutInt32 = 0;
+constexpr int kOutInt8Nhwc = 1;
+constexpr int kOutInt8VectC = 2;
 
 static int next_pow2(int v) {
   int p = 32;
@@ -596,7 +769,8 @@ static int next_pow2(int v) {
 }
 
 // Fills the launch geometry; false if the shape does not fit the kernel.
-static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, ConvGeom &g, int &cblk) {
+static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_kind, ConvGeom &g,
+                          int &cblk) {
   const int32_t out_h = (s.h + 2 * s.pad_h - s.dilation_h * (s.r - 1) - 1) / s.stride_h + 1;
   const int32_t out_w = (s.w + 2 * s.pad_w - s.dilation_w * (s.s - 1) - 1) / s.stride_w + 1;
   cblk = pick_cblk(s.c);
@@ -616,7 +790,7 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, ConvGeom
   g.dil_w = s.dilation_w;
   g.cblocks = (s.c + cblk - 1) / cblk;
   g.kblocks = s.r * s.s * g.cblocks;
-  g.bn = pick_bn(s.k);
+  g.bn = pick_bn(s.k, out_kind == kOutInt8VectC ? 32 : 16);
   g.pair = pair ? 1 : 0;
   g.acc_stride = (g.bn + 31) / 32 * 32;
   g.tmem_cols = next_pow2(2 * g.acc_stride);
@@ -670,13 +844,19 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, ConvGeom
   // TMA output stores: GENERIC rows are contiguous in NHWK; the row pitch
   // 4*K must be a multiple of 16 bytes; a 32-column block must not reach into
   // the next N tile (columns >= K are clipped, columns of a neighbour are not).
-  g.tma_store = mode == kModeGeneric && s.k % 4 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
+  // int8 NHWC: rows of K bytes (K % 16 == 0), 32-column blocks.
+  if (out_kind == kOutInt32)
+    g.tma_store = mode == kModeGeneric && s.k % 4 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
+  else if (out_kind == kOutInt8Nhwc)
+    g.tma_store = mode == kModeGeneric && s.k % 16 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
+  else
+    g.tma_store = 0;
   return true;
 }
 
-template <int CBLK, int MODE, bool PAIR>
+template <int CBLK, int MODE, bool PAIR, bool REQ>
 static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, const int8_t *x,
-                                const int8_t *w, const int32_t *b, int32_t *y,
+                                const int8_t *w, const int32_t *b, void *y, const Requant &rq,
                                 cudaStream_t stream) {
   DeviceInfo &dev = device_info();
   CUtensorMap maps[3];
@@ -691,11 +871,12 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   if (st != INT8CONV_OK) return st;
   maps[2] = CUtensorMap{};
   if (g.tma_store) {
-    st = output_map_tiled(y, g.M, g.K, &maps[2]);
+    st = REQ ? output_map_i8(static_cast<int8_t *>(y), g.M, g.K, &maps[2])
+             : output_map_tiled(static_cast<int32_t *>(y), g.M, g.K, &maps[2]);
     if (st != INT8CONV_OK) return st;
   }
   const SmemPlan plan = smem_plan(CBLK, b_rows, SHIFT ? g.a_rows : kBlockM, g.a_stages, g.stages);
-  auto kernel = conv_kernel<CBLK, MODE, PAIR>;
+  auto kernel = conv_kernel<CBLK, MODE, PAIR, REQ>;
   // At least half an SM's shared memory: one CTA per SM, so a CTA never waits
   // for another's TMEM columns.
   const uint32_t smem_bytes = plan.total > kOneCtaPerSm ? plan.total : kOneCtaPerSm;
@@ -712,7 +893,7 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
                         : (g.num_tiles < dev.sm_count ? g.num_tiles : dev.sm_count);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kernel_threads<REQ>(), 1, 1);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -724,65 +905,88 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = PAIR ? 2 : 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], g, b, y, ctl);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], g, b,
+                                             static_cast<int32_t *>(y), ctl, rq);
   note_launch();
   return err == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
 }
 
-template <int MODE, bool PAIR>
+template <int MODE, bool PAIR, bool REQ>
 static int8conv_status launch_cblk(const int8conv_shape &s, const ConvGeom &g, int cblk,
-                                   const int8_t *x, const int8_t *w, const int32_t *b,
-                                   int32_t *y, cudaStream_t stream) {
+                                   const int8_t *x, const int8_t *w, const int32_t *b, void *y,
+                                   const Requant &rq, cudaStream_t stream) {
   switch (cblk) {
     case 128:
-      return launch_t<128, MODE, PAIR>(s, g, x, w, b, y, stream);
+      return launch_t<128, MODE, PAIR, REQ>(s, g, x, w, b, y, rq, stream);
     case 64:
-      return launch_t<64, MODE, PAIR>(s, g, x, w, b, y, stream);
+      return launch_t<64, MODE, PAIR, REQ>(s, g, x, w, b, y, rq, stream);
     default:
-      return launch_t<32, MODE, PAIR>(s, g, x, w, b, y, stream);
+      return launch_t<32, MODE, PAIR, REQ>(s, g, x, w, b, y, rq, stream);
   }
 }
 
 // CTA pairs halve the filter bytes per output row.  Measured on B200 they pay
-// off when the filter tile is the full 256 columns and there are at least two
-// waves of 256-row tiles (5a: 357 vs 403 us, 5b: 92 vs 102 us); narrower or
-// smaller layers run faster as single CTAs (3b: 17 vs 23 us, 2: 17 vs 20 us).
-static bool use_pair(const int8conv_shape &s, int mode) {
+// off when the filter tile is the full 256 columns, there is at least one wave
+// of 256-row tiles, and either the reduction is deep (R*S*C >= 1024: 5a 354 vs
+// 401 us, 5b 92 vs 102 us) or there are many waves (big_1x1_s1, 4096 tiles:
+// 262 vs 266 us).  Narrower, shallower or smaller layers run faster as single
+// CTAs (3b: 17 vs 23 us, nonmultiple8_k255: 61 vs 65 us, batch16 bottleneck
+// expand: 24 vs 27 us).
+static bool use_pair(const int8conv_shape &s, int mode, int out_kind) {
   const int pairing = pairing_mode();
   if (pairing == 1) return false;
   ConvGeom g;
   int cblk = 0;
-  if (!plan_geometry(s, mode, true, g, cblk)) return false;
+  if (!plan_geometry(s, mode, true, out_kind, g, cblk)) return false;
   if (pairing == 2) return true;
-  return g.bn == 256 && g.num_tiles >= device_info().sm_count;
+  const int64_t reduction = static_cast<int64_t>(s.r) * s.s * s.c;
+  return g.bn == 256 && g.num_tiles >= device_info().sm_count &&
+         (reduction >= 1024 || g.num_tiles >= 1024);
 }
 
-template <int MODE>
+template <int MODE, bool REQ>
 static int8conv_status launch_mode(const int8conv_shape &s, const int8_t *x, const int8_t *w,
-                                   const int32_t *b, int32_t *y, cudaStream_t stream) {
+                                   const int32_t *b, void *y, const Requant &rq, int out_kind,
+                                   cudaStream_t stream) {
   ConvGeom g;
   int cblk = 0;
-  if (use_pair(s, MODE)) {
-    if (!plan_geometry(s, MODE, true, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
-    return launch_cblk<MODE, true>(s, g, cblk, x, w, b, y, stream);
+  if (use_pair(s, MODE, out_kind)) {
+    if (!plan_geometry(s, MODE, true, out_kind, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+    return launch_cblk<MODE, true, REQ>(s, g, cblk, x, w, b, y, rq, stream);
   }
-  if (!plan_geometry(s, MODE, false, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
-  return launch_cblk<MODE, false>(s, g, cblk, x, w, b, y, stream);
+  if (!plan_geometry(s, MODE, false, out_kind, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+  return launch_cblk<MODE, false, REQ>(s, g, cblk, x, w, b, y, rq, stream);
 }
 
 int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                     const int32_t *b, int32_t *y, cudaStream_t stream) {
-  return launch_mode<kModeGeneric>(s, x, w, b, y, stream);
+  return launch_mode<kModeGeneric, false>(s, x, w, b, y, Requant{}, kOutInt32, stream);
 }
 
 int8conv_status launch_strip_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                   const int32_t *b, int32_t *y, cudaStream_t stream) {
-  return launch_mode<kModeStrip>(s, x, w, b, y, stream);
+  return launch_mode<kModeStrip, false>(s, x, w, b, y, Requant{}, kOutInt32, stream);
 }
 
 int8conv_status launch_halo_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                  const int32_t *b, int32_t *y, cudaStream_t stream) {
-  return launch_mode<kModeHalo>(s, x, w, b, y, stream);
+  return launch_mode<kModeHalo, false>(s, x, w, b, y, Requant{}, kOutInt32, stream);
+}
+
+int8conv_status launch_conv_requant(int strategy, const int8conv_shape &s, const int8_t *x,
+                                    const int8_t *w, const int32_t *b, const Requant &rq,
+                                    int8_t *y, cudaStream_t stream) {
+  const int out_kind = rq.layout == 1 ? kOutInt8VectC : kOutInt8Nhwc;
+  switch (strategy) {
+    case INT8CONV_GENERIC:
+      return launch_mode<kModeGeneric, true>(s, x, w, b, y, rq, out_kind, stream);
+    case INT8CONV_STRIP:
+      return launch_mode<kModeStrip, true>(s, x, w, b, y, rq, out_kind, stream);
+    case INT8CONV_HALO:
+      return launch_mode<kModeHalo, true>(s, x, w, b, y, rq, out_kind, stream);
+    default:
+      return INT8CONV_NOT_ELIGIBLE;
+  }
 }
 
 }  // namespace i8c

@@ -12,7 +12,10 @@
 //   * same first 16 CSV columns in the same order (conv_lab.cu:223-230), then
 //     the appended ones: eligible_halo, eligible_splitk, halo_ms, splitk_ms,
 //     halo_correct, splitk_correct, gpus, tops, roofline_frac, oracle_ms,
-//     oracle_threads, graph_ms.
+//     oracle_threads, graph_ms, selected (the family int8conv_select picks),
+//     epilogue.
+// --epilogue int8 | int8x32 times int8conv_launch_requant (NHWC or cuDNN's
+// NCHW_VECT_C int8 output) with seeded per-channel multipliers and exponents.
 // Validation compares EVERY output element (the reference checks 2048
 // strided samples above 65536 outputs, conv_lab.cu:72-77) against a direct
 // host convolution with the loop nest of conv_lab.cu:39-66;
@@ -28,6 +31,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
+#include <functional>
 #include <iomanip>
 #include <iostream>
 #include <random>
@@ -37,6 +41,7 @@
 #include <vector>
 
 #include "int8conv.h"
+#include "requant.cuh"
 
 namespace {
 
@@ -76,13 +81,15 @@ struct Options {
   bool graph = true;
   int pairing = 0;
   long long validate_samples = 0;  // 0: every output
+  std::string epilogue = "int32";  // int32 | int8 (NHWC) | int8x32 (NCHW_VECT_C)
 };
 
 [[noreturn]] void usage() {
   std::cerr << "usage: conv_lab [--strategy generic|strip|halo|splitk|both|all|auto] [--csv] "
                "[--warmup N] [--iterations N] [--case NAME] [--config CSV] "
                "[--values full|reference] [--seed S] [--batch N] [--peak-tops T] "
-               "[--no-graph] [--pairing auto|single|pair] [--validate-samples N]\n";
+               "[--no-graph] [--pairing auto|single|pair] [--validate-samples N] "
+               "[--epilogue int32|int8|int8x32]\n";
   std::exit(EXIT_FAILURE);
 }
 
@@ -106,6 +113,7 @@ Options parse_options(int argc, char **argv) {
     else if (arg == "--batch") o.batch = std::stoi(value());
     else if (arg == "--peak-tops") o.peak_tops = std::stod(value());
     else if (arg == "--validate-samples") o.validate_samples = std::stoll(value());
+    else if (arg == "--epilogue") o.epilogue = value();
     else if (arg == "--pairing") {
       const std::string v = value();
       o.pairing = v == "auto" ? 0 : v == "single" ? 1 : v == "pair" ? 2 : -1;
@@ -114,7 +122,8 @@ Options parse_options(int argc, char **argv) {
   }
   const std::vector<std::string> ok = {"generic", "strip", "halo", "splitk", "both", "all", "auto"};
   if (std::find(ok.begin(), ok.end(), o.strategy) == ok.end() || o.warmup < 0 ||
-      o.iterations <= 0 || (o.values != "full" && o.values != "reference") || o.batch < 0) {
+      o.iterations <= 0 || (o.values != "full" && o.values != "reference") || o.batch < 0 ||
+      (o.epilogue != "int32" && o.epilogue != "int8" && o.epilogue != "int8x32")) {
     std::cerr << "invalid benchmark options\n";
     std::exit(EXIT_FAILURE);
   }
@@ -186,10 +195,13 @@ int32_t direct_value(const int8conv_shape &s, const int8conv_dims &d, const std:
 // `samples` is 0 (the default; the reference checks only 2048 strided samples
 // above 65536 outputs, conv_lab.cu:72-77), else the first and last output
 // rows plus `samples` seeded random outputs.
+// `expect` maps the int32 value and its channel to the value the epilogue
+// writes (the identity for int32 output, the requantisation for int8).
 bool validate_all(const int8conv_shape &s, const int8conv_dims &d,
                   const std::vector<int8_t> &x, const std::vector<int8_t> &w,
                   const std::vector<int32_t> &b, const std::vector<int32_t> &y,
-                  const char *label, int threads, double &ms, long long samples = 0) {
+                  const char *label, int threads, double &ms, long long samples,
+                  const std::function<int32_t(int32_t, int)> &expect) {
   const auto t0 = std::chrono::steady_clock::now();
   std::vector<long long> first_bad(threads, -1);
   std::vector<std::thread> pool;
@@ -208,7 +220,8 @@ bool validate_all(const int8conv_shape &s, const int8conv_dims &d,
       if (samples > 0) {
         for (size_t i = t; i < picks.size(); i += threads) {
           const int64_t idx = picks[i];
-          if (y[idx] != direct_value(s, d, x, w, b, idx / s.k, static_cast<int>(idx % s.k))) {
+          const int k = static_cast<int>(idx % s.k);
+          if (y[idx] != expect(direct_value(s, d, x, w, b, idx / s.k, k), k)) {
             first_bad[t] = idx;
             return;
           }
@@ -217,7 +230,7 @@ bool validate_all(const int8conv_shape &s, const int8conv_dims &d,
       }
       for (int64_t m = t; m < d.gemm_m; m += threads) {
         for (int k = 0; k < s.k; ++k) {
-          if (y[m * s.k + k] != direct_value(s, d, x, w, b, m, k)) {
+          if (y[m * s.k + k] != expect(direct_value(s, d, x, w, b, m, k), k)) {
             first_bad[t] = m * s.k + k;
             return;
           }
@@ -337,11 +350,33 @@ int main(int argc, char **argv) {
   for (auto &v : input) v = static_cast<int8_t>(values(rng));
   for (auto &v : filter) v = static_cast<int8_t>(values(rng));
   for (auto &v : bias) v = bias_values(rng);
+  // int8 epilogues: per-channel Q31 multipliers in [2^30, 2^31) and
+  // exponents in [-13, -8], which spread the accumulators over int8.
+  const bool int8_out = options.epilogue != "int32";
+  const int layout = options.epilogue == "int8x32" ? INT8CONV_LAYOUT_NCHW_VECT_C
+                                                    : INT8CONV_LAYOUT_NHWC;
+  std::vector<int32_t> multiplier(shape.k), exponent(shape.k);
+  std::uniform_int_distribution<int32_t> mult_values(1 << 30, 0x7fffffff);
+  std::uniform_int_distribution<int32_t> exp_values(-13, -8);
+  for (auto &v : multiplier) v = mult_values(rng);
+  for (auto &v : exponent) v = exp_values(rng);
 
   DeviceBuffer<int8_t> d_input(input.size());
   DeviceBuffer<int8_t> d_filter(filter.size());
   DeviceBuffer<int32_t> d_bias(bias.size());
-  DeviceBuffer<int32_t> d_output(d.output_elements);
+  DeviceBuffer<int32_t> d_output(int8_out ? 1 : d.output_elements);
+  DeviceBuffer<int8_t> d_output8(int8_out ? d.output_elements : 1);
+  DeviceBuffer<int32_t> d_multiplier(shape.k), d_exponent(shape.k);
+  check(cudaMemcpy(d_multiplier.get(), multiplier.data(), shape.k * sizeof(int32_t),
+                   cudaMemcpyHostToDevice),
+        "copy multipliers");
+  check(cudaMemcpy(d_exponent.get(), exponent.data(), shape.k * sizeof(int32_t),
+                   cudaMemcpyHostToDevice),
+        "copy exponents");
+  const int8conv_requant requant{d_multiplier.get(), d_exponent.get(), 0, 0, layout};
+  auto expect = [&](int32_t v, int k) -> int32_t {
+    return int8_out ? i8c::rq_apply(v, multiplier[k], exponent[k], 0, false) : v;
+  };
   check(cudaMemcpy(d_input.get(), input.data(), input.size(), cudaMemcpyHostToDevice), "copy input");
   check(cudaMemcpy(d_filter.get(), filter.data(), filter.size(), cudaMemcpyHostToDevice),
         "copy filter");
@@ -365,7 +400,8 @@ int main(int argc, char **argv) {
   const int threads = std::max(1u, std::thread::hardware_concurrency());
   std::vector<int32_t> output(d.output_elements);
   for (int f = 0; f < INT8CONV_NUM_STRATEGIES; ++f) {
-    eligible[f] = int8conv_eligible(&shape, f) != 0;
+    eligible[f] = int8conv_eligible(&shape, f) != 0 &&
+                  (layout != INT8CONV_LAYOUT_NCHW_VECT_C || !int8_out || shape.k % 32 == 0);
     ms[f] = -1.0f;
     graph_ms[f] = -1.0f;
     correct[f] = true;
@@ -374,8 +410,11 @@ int main(int argc, char **argv) {
     DeviceBuffer<uint8_t> workspace(ws_bytes);
     auto launch_on = [&](cudaStream_t stream) {
       const int8conv_status st =
-          int8conv_launch(f, &shape, d_input.get(), d_filter.get(), d_bias.get(),
-                          d_output.get(), workspace.get(), ws_bytes, stream);
+          int8_out ? int8conv_launch_requant(f, &shape, d_input.get(), d_filter.get(),
+                                             d_bias.get(), &requant, d_output8.get(),
+                                             workspace.get(), ws_bytes, stream)
+                   : int8conv_launch(f, &shape, d_input.get(), d_filter.get(), d_bias.get(),
+                                     d_output.get(), workspace.get(), ws_bytes, stream);
       if (st != INT8CONV_OK) {
         std::cerr << int8conv_strategy_name(f) << " launch: " << int8conv_status_string(st)
                   << '\n';
@@ -383,7 +422,10 @@ int main(int argc, char **argv) {
       }
     };
     auto launch = [&] { launch_on(nullptr); };
-    check(cudaMemset(d_output.get(), 0xA5, d.output_elements * sizeof(int32_t)), "poison");
+    if (int8_out)
+      check(cudaMemset(d_output8.get(), 0xA5, d.output_elements), "poison");
+    else
+      check(cudaMemset(d_output.get(), 0xA5, d.output_elements * sizeof(int32_t)), "poison");
     launch();
     check(cudaGetLastError(), "launch");
     check(cudaDeviceSynchronize(), "synchronize");
@@ -392,12 +434,30 @@ int main(int argc, char **argv) {
       correct[f] = false;
       continue;
     }
-    check(cudaMemcpy(output.data(), d_output.get(), output.size() * sizeof(int32_t),
-                     cudaMemcpyDeviceToHost),
-          "copy output");
+    if (int8_out) {
+      // Back to NHWK order, widened, so one validator serves every epilogue.
+      std::vector<int8_t> out8(d.output_elements);
+      check(cudaMemcpy(out8.data(), d_output8.get(), out8.size(), cudaMemcpyDeviceToHost),
+            "copy output");
+      const int64_t pq = static_cast<int64_t>(d.out_h) * d.out_w;
+      for (int64_t i = 0; i < d.output_elements; ++i) {
+        const int64_t m = i / shape.k;
+        const int k = static_cast<int>(i % shape.k);
+        const int64_t src =
+            layout == INT8CONV_LAYOUT_NHWC
+                ? i
+                : ((m / pq * (shape.k / 32) + k / 32) * pq + m % pq) * 32 + k % 32;
+        output[i] = out8[src];
+      }
+    } else {
+      check(cudaMemcpy(output.data(), d_output.get(), output.size() * sizeof(int32_t),
+                       cudaMemcpyDeviceToHost),
+            "copy output");
+    }
     double vms = 0;
     correct[f] = validate_all(shape, d, input, filter, bias, output,
-                              int8conv_strategy_name(f), threads, vms, options.validate_samples);
+                              int8conv_strategy_name(f), threads, vms, options.validate_samples,
+                              expect);
     oracle_ms = std::max(oracle_ms, vms);
     if (!correct[f]) continue;
     ms[f] = measure(launch, options.warmup, options.iterations);
@@ -417,7 +477,7 @@ int main(int argc, char **argv) {
     std::cout << "case,n,h,w,c,k,r,s,out_h,out_w,eligible_strip,generic_ms,strip_ms,winner,"
                  "generic_correct,strip_correct,eligible_halo,eligible_splitk,halo_ms,splitk_ms,"
                  "halo_correct,splitk_correct,gpus,tops,roofline_frac,oracle_ms,oracle_threads,"
-                 "graph_ms\n";
+                 "graph_ms,selected,epilogue\n";
     std::cout << options.case_name << ',' << shape.n << ',' << shape.h << ',' << shape.w << ','
               << shape.c << ',' << shape.k << ',' << shape.r << ',' << shape.s << ',' << d.out_h
               << ',' << d.out_w << ',' << (eligible[INT8CONV_STRIP] ? 1 : 0) << ','
@@ -428,7 +488,9 @@ int main(int argc, char **argv) {
               << ms[INT8CONV_SPLITK] << ',' << (correct[INT8CONV_HALO] ? 1 : 0) << ','
               << (correct[INT8CONV_SPLITK] ? 1 : 0) << ",1," << fmt(tops) << ','
               << fmt(tops < 0 ? -1.0 : tops / options.peak_tops) << ',' << fmt(oracle_ms) << ','
-              << threads << ',' << (winner < 0 ? -1.0f : graph_ms[winner]) << '\n';
+              << threads << ',' << (winner < 0 ? -1.0f : graph_ms[winner]) << ','
+              << int8conv_strategy_name(int8conv_select(&shape)) << ',' << options.epilogue
+              << '\n';
   } else {
     std::cout << options.case_name << ":";
     for (int f = 0; f < INT8CONV_NUM_STRATEGIES; ++f) {

@@ -9,6 +9,7 @@
 
 #include "conv_common.h"
 #include "int8conv.h"
+#include "requant.cuh"
 
 namespace i8c {
 
@@ -52,6 +53,20 @@ int8conv_status filter_map_tiled(const int8conv_shape &s, const int8_t *w, int c
 // Tiled tensor map over the NHWK int32 output viewed as [M][K], box 32 x 32,
 // 128-byte swizzle (the epilogue's staging layout).
 int8conv_status output_map_tiled(int32_t *y, int64_t m, int k, CUtensorMap *map);
+
+// Tiled tensor map over the NHWC int8 requantised output viewed as [M][K]
+// (K % 16 == 0), box 32 x 32, no swizzle: one epilogue warp's 32 rows x 32
+// columns per store.
+int8conv_status output_map_i8(int8_t *y, int64_t m, int k, CUtensorMap *map);
+
+// Requantised-output variants of the family launchers (`rq` non-null; `y`
+// int8 in rq->layout).
+int8conv_status launch_conv_requant(int strategy, const int8conv_shape &s, const int8_t *x,
+                                    const int8_t *w, const int32_t *b, const Requant &rq,
+                                    int8_t *y, cudaStream_t stream);
+int8conv_status launch_splitk_requant(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                      const int32_t *b, const Requant &rq, int8_t *y,
+                                      cudaStream_t stream);
 
 // Family launchers (valid, eligible shape; pointers already checked).
 int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,

@@ -61,12 +61,12 @@ struct SplitSwizzle<32> {
   static constexpr Layout kLayout = Layout::kSw32;
 };
 
-template <int CBLK>
+template <int CBLK, bool REQ>
 __global__ void __launch_bounds__(kSplitThreads, 1)
     splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
                   const __grid_constant__ CUtensorMap tmap_w, const SplitGeom sg,
                   const int32_t *__restrict__ bias, int32_t *__restrict__ out,
-                  const RunCtl ctl) {
+                  const RunCtl ctl, const Requant rq) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -251,6 +251,38 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       acc.z += v.z;
       acc.w += v.w;
     }
+    if constexpr (REQ) {
+      // Four int8 outputs of one row: NHWC bytes m*K + col.., or one quarter
+      // of a 32-channel vector in NCHW_VECT_C (K % 32 == 0).
+      const int32_t a4[4] = {acc.x, acc.y, acc.z, acc.w};
+      const int32_t lo = rq.relu ? rq.zero_point : -128;
+      int32_t y4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool in = col + j < g.K;
+        y4[j] = in ? rq_apply_dev(static_cast<int32_t>(static_cast<uint32_t>(a4[j]) +
+                                                       static_cast<uint32_t>(__ldg(bias + col + j))),
+                                  rq_channel(__ldg(rq.multiplier + col + j),
+                                             __ldg(rq.exponent + col + j)),
+                                  rq.zero_point, lo)
+                   : 0;
+      }
+      int8_t *out8 = reinterpret_cast<int8_t *>(out);
+      if (rq.layout == 1) {
+        const int img = m / g.PQ;
+        const int pq = m - img * g.PQ;
+        *reinterpret_cast<uint32_t *>(
+            out8 + ((static_cast<int64_t>(img) * (g.K >> 5) + (col >> 5)) * g.PQ + pq) * 32 +
+            (col & 31)) = rq_pack4(y4[0], y4[1], y4[2], y4[3]);
+      } else if (vec_k) {
+        *reinterpret_cast<uint32_t *>(out8 + static_cast<int64_t>(m) * g.K + col) =
+            rq_pack4(y4[0], y4[1], y4[2], y4[3]);
+      } else {
+        for (int j = 0; j < 4 && col + j < g.K; ++j)
+          out8[static_cast<int64_t>(m) * g.K + col + j] = static_cast<int8_t>(y4[j]);
+      }
+      continue;
+    }
     int32_t *o = out + static_cast<int64_t>(m) * g.K + col;
     if (vec_k) {
       const int4 bb = __ldg(reinterpret_cast<const int4 *>(bias + col));
@@ -276,8 +308,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 
 static int split_cblk(int c) { return i8c_channel_block(c); }
 
-// Plans a split-K launch; false if the shape has too little reduction to split.
-static bool plan_split(const int8conv_shape &s, int sm_count, SplitGeom &sg, int &cblk) {
+// Plans a split-K launch; false if the shape has too little reduction to
+// split.  `clusters[c]` = clusters of size c that can be resident at once.
+static bool plan_split(const int8conv_shape &s, const int32_t *clusters, SplitGeom &sg,
+                       int &cblk) {
   const int32_t out_h = (s.h + 2 * s.pad_h - s.dilation_h * (s.r - 1) - 1) / s.stride_h + 1;
   const int32_t out_w = (s.w + 2 * s.pad_w - s.dilation_w * (s.s - 1) - 1) / s.stride_w + 1;
   cblk = split_cblk(s.c);
@@ -307,9 +341,9 @@ static bool plan_split(const int8conv_shape &s, int sm_count, SplitGeom &sg, int
   g.m_tiles = (g.M + kBlockM - 1) / kBlockM;
   g.n_tiles = (s.k + g.bn - 1) / g.bn;
   g.num_tiles = g.m_tiles * g.n_tiles;
-  int splits = sm_count / g.num_tiles;
-  if (splits > kMaxSplits) splits = kMaxSplits;
-  if (splits > g.kblocks) splits = g.kblocks;
+  // The largest split whose clusters all run in one wave; with too many
+  // tiles for that, pairs of CTAs in several waves.
+  int splits = i8c_split_count(g.num_tiles, g.kblocks, clusters);
   if (splits < 2) splits = 2;
   sg.splits = splits;
   sg.part_pitch = 4 * g.bn + 16;
@@ -332,13 +366,14 @@ static bool plan_split(const int8conv_shape &s, int sm_count, SplitGeom &sg, int
 bool splitk_eligible_runtime(const int8conv_shape &s) {
   SplitGeom sg;
   int cblk = 0;
-  return plan_split(s, 148, sg, cblk);
+  const int32_t b200[9] = I8C_B200_CLUSTERS;
+  return plan_split(s, b200, sg, cblk);
 }
 
-template <int CBLK>
+template <int CBLK, bool REQ>
 static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &sg,
                                       const int8_t *x, const int8_t *w, const int32_t *b,
-                                      int32_t *y, cudaStream_t stream) {
+                                      void *y, const Requant &rq, cudaStream_t stream) {
   CUtensorMap maps[2];
   int8conv_status st = activation_map_im2col(s, x, CBLK, kBlockM, sg.g.Q, sg.g.P, &maps[0]);
   if (st != INT8CONV_OK) return st;
@@ -346,7 +381,7 @@ static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &
   if (st != INT8CONV_OK) return st;
   const uint32_t total = 1024 + sg.ring_bytes + (2 * sg.g.stages + 1) * 8 + 16;
   const uint32_t smem = total > kMaxSmem / 2 + 1024 ? total : kMaxSmem / 2 + 1024;
-  auto kernel = splitk_kernel<CBLK>;
+  auto kernel = splitk_kernel<CBLK, REQ>;
   static std::atomic<uint32_t> smem_set[64];
   std::atomic<uint32_t> &slot = smem_set[device_info().device & 63];
   if (slot.load(std::memory_order_relaxed) < smem) {
@@ -368,24 +403,77 @@ static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], sg, b, y, run_ctl());
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], sg, b,
+                                             static_cast<int32_t *>(y), run_ctl(), rq);
   note_launch();
   return err == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
 }
 
-int8conv_status launch_splitk_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
-                                   const int32_t *b, int32_t *y, cudaStream_t stream) {
+// Resident clusters per cluster size on the current device, queried once
+// per device (cudaOccupancyMaxActiveClusters; one CTA per SM, like every
+// split-K launch).  Falls back to the B200 table if the query fails.
+static const int32_t *cluster_table() {
+  static int32_t table[64][9];
+  static std::atomic<int> ready[64];
+  DeviceInfo &dev = device_info();
+  const int d = dev.device & 63;
+  if (ready[d].load(std::memory_order_acquire)) return table[d];
+  const int32_t b200[9] = I8C_B200_CLUSTERS;
+  int32_t t[9];
+  auto kernel = splitk_kernel<128, false>;
+  const bool attr_ok = ensure_smem_attr(reinterpret_cast<const void *>(kernel), kMaxSmem);
+  for (int c = 0; c < 9; ++c) {
+    t[c] = b200[c];
+    if (c < 2 || !attr_ok) continue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c * 16, 1, 1);
+    cfg.blockDim = dim3(kSplitThreads, 1, 1);
+    cfg.dynamicSmemBytes = kMaxSmem / 2 + 1024;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = c;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess && n > 0)
+      t[c] = n;
+    else
+      cudaGetLastError();
+  }
+  t[1] = dev.sm_count;
+  for (int c = 0; c < 9; ++c) table[d][c] = t[c];
+  ready[d].store(1, std::memory_order_release);
+  return table[d];
+}
+
+template <bool REQ>
+static int8conv_status launch_split(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                    const int32_t *b, void *y, const Requant &rq,
+                                    cudaStream_t stream) {
   SplitGeom sg;
   int cblk = 0;
-  if (!plan_split(s, device_info().sm_count, sg, cblk)) return INT8CONV_NOT_ELIGIBLE;
+  if (!plan_split(s, cluster_table(), sg, cblk)) return INT8CONV_NOT_ELIGIBLE;
   switch (cblk) {
     case 128:
-      return launch_split_t<128>(s, sg, x, w, b, y, stream);
+      return launch_split_t<128, REQ>(s, sg, x, w, b, y, rq, stream);
     case 64:
-      return launch_split_t<64>(s, sg, x, w, b, y, stream);
+      return launch_split_t<64, REQ>(s, sg, x, w, b, y, rq, stream);
     default:
-      return launch_split_t<32>(s, sg, x, w, b, y, stream);
+      return launch_split_t<32, REQ>(s, sg, x, w, b, y, rq, stream);
   }
+}
+
+int8conv_status launch_splitk_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                   const int32_t *b, int32_t *y, cudaStream_t stream) {
+  return launch_split<false>(s, x, w, b, y, Requant{}, stream);
+}
+
+int8conv_status launch_splitk_requant(const int8conv_shape &s, const int8_t *x, const int8_t *w,
+                                      const int32_t *b, const Requant &rq, int8_t *y,
+                                      cudaStream_t stream) {
+  return launch_split<true>(s, x, w, b, y, rq, stream);
 }
 
 }  // namespace i8c

@@ -9,6 +9,14 @@ family is run (--strategy all); rows are written incrementally after each case
 (sweep.py:58-61), so an interrupted sweep keeps what it measured.  The CSV is
 conv_lab's: the reference's 16 columns, then the appended ones.
 
+--arch keeps the reference's flag; the library is built for sm_100a only, so
+any other value is an error.  --with-cudnn keeps the reference's merge columns
+(sweep.py:44-56: dispatch_ms, cudnn_ms, cudnn_over_dispatch,
+comparison_contract).  cuDNN is not part of this engine, so cudnn_ms stays
+empty and the contract reads "cudnn_not_built"; dispatch_ms maps the winner of
+all four families to its time (the reference's mapping, sweep.py:48, knows
+only strip and generic).
+
     python -m int8_kernel_lab_b200.sweep --cases cfg2_mid_3x3,big_3x3_s1 \\
         --output build/dispatch_measurements.csv
 """
@@ -19,6 +27,13 @@ import sys
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
+
+
+def dispatch_ms(row: dict) -> str:
+    """The winner's per-launch time, for any of the four families."""
+    column = {"generic": "generic_ms", "strip": "strip_ms", "halo": "halo_ms",
+              "splitk": "splitk_ms"}.get(row["winner"])
+    return row[column] if column else ""
 
 
 def main(argv=None) -> int:
@@ -34,7 +49,12 @@ def main(argv=None) -> int:
     ap.add_argument("--full-validate-ops", type=float, default=2e11,
                     help="shapes with more ops validate 200000 sampled outputs, not all")
     ap.add_argument("--conv-lab", default=str(PKG / "lib" / "conv_lab"))
+    ap.add_argument("--arch", default="sm_100a")
+    ap.add_argument("--with-cudnn", action="store_true")
+    ap.add_argument("--cudnn-root", default="")
     args = ap.parse_args(argv)
+    if args.arch not in ("sm_100a", "sm_100"):
+        raise SystemExit(f"--arch {args.arch}: this engine is built for sm_100a only")
     with open(args.configs, newline="") as stream:
         rows = list(csv.DictReader(stream))
     requested = args.cases.split(",") if args.cases else [r["name"] for r in rows]
@@ -65,7 +85,11 @@ def main(argv=None) -> int:
         if len(lines) < 2:
             print(f"{case}: conv_lab failed (exit {result.returncode})", file=sys.stderr)
             continue
-        measurements.append(next(csv.DictReader(lines)))
+        measurement = next(csv.DictReader(lines))
+        if args.with_cudnn:
+            measurement.update(dispatch_ms=dispatch_ms(measurement), cudnn_ms="",
+                               cudnn_over_dispatch="", comparison_contract="cudnn_not_built")
+        measurements.append(measurement)
         with open(args.output, "w", newline="") as stream:
             writer = csv.DictWriter(stream, fieldnames=measurements[0].keys())
             writer.writeheader()

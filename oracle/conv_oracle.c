@@ -122,3 +122,64 @@ int oracle_max_threads(void) {
   return 1;
 #endif
 }
+
+/* ---- requantised int8 output (no reference counterpart) -------------------
+ * Restates the published gemmlowp / TensorFlow Lite fixed-point requantisation
+ * (SaturatingRoundingDoublingHighMul, then RoundingDivideByPOT) with plain C
+ * integer division, independently of the engine's shift-based kernel code:
+ *   e = clamp(exponent, -31, 31); t = e > 0 ? saturate(t * 2^e) : t
+ *   u = (t*mult + (t*mult >= 0 ? 2^30 : 1 - 2^30)) / 2^31   (C division truncates)
+ *       INT32_MIN * INT32_MIN -> INT32_MAX
+ *   v = e < 0 ? u / 2^-e rounded half away from zero : u
+ *   y = clamp(v + zero_point, relu ? zero_point : -128, 127)             */
+static int32_t oracle_srdhm(int32_t a, int32_t b) {
+  if (a == INT32_MIN && b == INT32_MIN) return INT32_MAX;
+  const int64_t ab = (int64_t)a * (int64_t)b;
+  const int64_t nudge = ab >= 0 ? ((int64_t)1 << 30) : (1 - ((int64_t)1 << 30));
+  return (int32_t)((ab + nudge) / ((int64_t)1 << 31));
+}
+
+static int32_t oracle_div_pot_round(int32_t x, int e) {
+  const int64_t d = (int64_t)1 << e;
+  int64_t q = (int64_t)x / d;
+  const int64_t r = (int64_t)x % d;
+  const int64_t twice = r < 0 ? -2 * r : 2 * r;
+  if (twice >= d) q += x < 0 ? -1 : 1;
+  return (int32_t)q;
+}
+
+int32_t oracle_requant_value(int32_t t, int32_t multiplier, int32_t exponent,
+                             int32_t zero_point, int32_t relu) {
+  int e = exponent;
+  if (e < -31) e = -31;
+  if (e > 31) e = 31;
+  if (e > 0) {
+    int64_t v = (int64_t)t;
+    for (int i = 0; i < e; ++i) v *= 2;
+    if (v > INT32_MAX) v = INT32_MAX;
+    if (v < INT32_MIN) v = INT32_MIN;
+    t = (int32_t)v;
+  }
+  int32_t u = oracle_srdhm(t, multiplier);
+  if (e < 0) u = oracle_div_pot_round(u, -e);
+  int64_t y = (int64_t)u + zero_point;
+  const int64_t lo = relu ? zero_point : -128;
+  if (y < lo) y = lo;
+  if (y > 127) y = 127;
+  return (int32_t)y;
+}
+
+/* NHWK int32 (accumulator + bias, as oracle_conv returns) -> NHWK int8. */
+void oracle_requant(const int32_t *acc, int64_t rows, int32_t k, const int32_t *multiplier,
+                    const int32_t *exponent, int32_t zero_point, int32_t relu, int8_t *out,
+                    int threads) {
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(threads)
+#endif
+  for (int64_t m = 0; m < rows; ++m)
+    for (int32_t c = 0; c < k; ++c)
+      out[m * k + c] = (int8_t)oracle_requant_value(acc[m * k + c], multiplier[c], exponent[c],
+                                                    zero_point, relu);
+  (void)threads;
+}

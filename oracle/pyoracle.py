@@ -49,6 +49,10 @@ def _lib() -> ctypes.CDLL:
     lib.oracle_out_h.argtypes = [SP]
     lib.oracle_out_w.argtypes = [SP]
     lib.oracle_max_threads.restype = ctypes.c_int
+    lib.oracle_requant.argtypes = [P, ctypes.c_int64, ctypes.c_int32, P, P, ctypes.c_int32,
+                                   ctypes.c_int32, P, ctypes.c_int]
+    lib.oracle_requant_value.argtypes = [ctypes.c_int32] * 5
+    lib.oracle_requant_value.restype = ctypes.c_int32
     return lib
 
 
@@ -127,3 +131,55 @@ def ref_cpu_rows(case: str, x, w, b, m_begin: int, m_end: int, threads: int):
         result = json.loads(proc.stdout.strip().splitlines()[-1])
         rows = np.fromfile(paths[3], dtype=np.int32)
     return rows, float(result["seconds"])
+
+
+# ---- requantised int8 output (no reference counterpart) ----------------------
+
+def requant(acc, k: int, multiplier, exponent, zero_point: int = 0, relu: bool = False,
+            threads: int = 0) -> np.ndarray:
+    """NHWK int32 (conv() output) -> NHWK int8 by the C restatement."""
+    acc = np.ascontiguousarray(acc, dtype=np.int32).reshape(-1)
+    mult = np.ascontiguousarray(multiplier, dtype=np.int32)
+    expo = np.ascontiguousarray(exponent, dtype=np.int32)
+    assert acc.size % k == 0 and mult.size == k and expo.size == k
+    out = np.empty(acc.size, dtype=np.int8)
+    lib().oracle_requant(acc.ctypes.data, acc.size // k, int(k), mult.ctypes.data,
+                         expo.ctypes.data, int(zero_point), int(bool(relu)), out.ctypes.data,
+                         int(threads))
+    return out
+
+
+def requant_value(t: int, multiplier: int, exponent: int, zero_point: int = 0,
+                  relu: bool = False) -> int:
+    return int(lib().oracle_requant_value(int(t), int(multiplier), int(exponent),
+                                          int(zero_point), int(bool(relu))))
+
+
+def requant_value_py(t: int, multiplier: int, exponent: int, zero_point: int = 0,
+                     relu: bool = False) -> int:
+    """Third restatement of the same rule with Python's unbounded integers:
+    the rounding steps written as exact rational rounding."""
+    e = max(-31, min(31, exponent))
+    if e > 0:
+        t = max(-2**31, min(2**31 - 1, t * 2**e))
+    if t == -2**31 and multiplier == -2**31:
+        u = 2**31 - 1
+    else:
+        ab = t * multiplier
+        num = ab + (2**30 if ab >= 0 else 1 - 2**30)
+        u = abs(num) // 2**31 * (1 if num >= 0 else -1)      # truncating division
+    if e < 0:
+        d = 2**-e
+        q, r = divmod(abs(u), d)                               # |u| = q*d + r
+        q += 1 if 2 * r >= d else 0                            # half away from zero
+        u = q if u >= 0 else -q
+    y = u + zero_point
+    y = max(zero_point if relu else -128, y)
+    return min(127, y)
+
+
+def to_nchw_vect_c(y_nhwk: np.ndarray, n: int, out_h: int, out_w: int, k: int) -> np.ndarray:
+    """NHWK int8 -> cuDNN INT8x32 NCHW_VECT_C [N][K/32][P][Q][32] (flat)."""
+    assert k % 32 == 0
+    y = np.asarray(y_nhwk).reshape(n, out_h, out_w, k // 32, 32)
+    return np.ascontiguousarray(y.transpose(0, 3, 1, 2, 4)).reshape(-1)

@@ -14,7 +14,7 @@ REFERENCE_COLUMNS = ["case", "n", "h", "w", "c", "k", "r", "s", "out_h", "out_w"
                      "generic_ms", "strip_ms", "winner", "generic_correct", "strip_correct"]
 APPENDED = ["eligible_halo", "eligible_splitk", "halo_ms", "splitk_ms", "halo_correct",
             "splitk_correct", "gpus", "tops", "roofline_frac", "oracle_ms", "oracle_threads",
-            "graph_ms"]
+            "graph_ms", "selected", "epilogue"]
 
 
 def run(*args):
@@ -24,6 +24,7 @@ def run(*args):
 @pytest.mark.parametrize("args", [
     ["--strategy", "fastest"], ["--iterations", "0"], ["--warmup", "-1"], ["--bogus"],
     ["--warmup"], ["--iterations", "x"], ["--pairing", "triple"], ["--values", "small"],
+    ["--epilogue", "fp8"],
 ])
 def test_bad_options_exit_nonzero(args):
     out = run(*args)
@@ -50,6 +51,7 @@ def test_csv_row_keeps_reference_columns(strategy):
     assert row["case"] == "smoke" and row["out_h"] == "16" and row["out_w"] == "16"
     assert row["generic_correct"] == "1" and row["strip_correct"] == "1"
     assert row["winner"] in ("generic", "strip", "halo", "splitk")
+    assert row["selected"] in ("generic", "strip", "halo", "splitk")
 
 
 @pytest.mark.gpu
@@ -58,3 +60,15 @@ def test_human_line_and_reference_values():
               "--warmup", "1")
     assert out.returncode == 0, out.stderr
     assert out.stdout.startswith("resnet_s3_3x3: generic ") and "winner" in out.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case, epilogue", [("cfg2_mid_3x3", "int8"), ("cfg2_mid_3x3", "int8x32"),
+                                            ("cfg4c_tail_k100", "int8")])
+def test_int8_epilogues_validate(case, epilogue):
+    out = run("--case", case, "--strategy", "all", "--epilogue", epilogue, "--csv",
+              "--iterations", "5", "--warmup", "2")
+    assert out.returncode == 0, out.stderr
+    row = next(csv.DictReader(io.StringIO(out.stdout)))
+    assert row["epilogue"] == epilogue
+    assert all(row[f + "_correct"] == "1" for f in ("generic", "strip", "halo", "splitk"))

@@ -172,6 +172,7 @@ def test_stream_argument_and_async(cuda):
     dx, dw, db = (torch.from_numpy(a).cuda() for a in (x, w, b))
     dy = torch.zeros(shape.output_elements, dtype=torch.int32, device="cuda")
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())  # the buffers' copies and fill
     with torch.cuda.stream(s):
         m.launch_generic(shape, dx, dw, db, dy, stream=s)
     s.synchronize()

@@ -73,3 +73,14 @@ def test_dispatch_policy_on_baseline():
     table = m.load_workloads()
     for name, fam in want.items():
         assert table[name].select() == fam, name
+
+
+def test_dispatch_needs_a_single_wave_split():
+    # Split-K only where its clusters fit in one wave of resident clusters
+    # (B200: 74 pairs, 45 triples, ..., 15 clusters of 7 or 8).  batch8_3x3 has
+    # 98 split tiles (two waves even as pairs) and lost to GENERIC 28.8 vs
+    # 18.2 us; darknet_down_52 (24 tiles) fits as clusters of 5.
+    table = m.load_workloads()
+    assert table["batch8_3x3"].select() == "generic"
+    for name in ("darknet_down_52", "cfg4a_deep_1x1", "darknet_head_13", "resnet_s4_3x3"):
+        assert table[name].select() == "splitk", name
