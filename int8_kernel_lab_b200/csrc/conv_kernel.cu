@@ -133,42 +133,19 @@ __device__ __forceinline__ void commit_to(uint64_t *bar) {
     umma_commit(bar);
 }
 
-// Bias plus requantisation of one thread's 32 accumulators (columns col0..,
-// this warp's row): four channels per word.  Columns at or past the tile
-// width or K get zero parameters; they are never stored.  `lo` is the lower
-// clamp (the zero point with ReLU, else -128).
-__device__ __forceinline__ void requant_block(const uint32_t (&v)[32], const int32_t *bias,
-                                              const Requant &rq, int col0, int cols_left,
-                                              int K, int32_t lo, uint32_t (&w8)[8]) {
-  const bool vec4 = (K & 3) == 0;
+// Requantisation of one thread's 32 accumulators (this warp's row, a
+// 32-column block): four channels per word.  `table` holds the block's 32
+// channel entries (rq_entry, bias included); every lane reads each entry with
+// one broadcast load.  `lo` is the lower clamp (the zero point with ReLU,
+// else -128).
+__device__ __forceinline__ void requant_block(const uint32_t (&v)[32], const int4 *table,
+                                              int32_t zero_point, int32_t lo,
+                                              uint32_t (&w8)[8]) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const int c = col0 + 4 * j;
-    int32_t bb[4], mm[4], ee[4];
-    if (vec4) {
-      const bool in = 4 * j < cols_left && c < K;
-      const int4 b4 = in ? __ldg(reinterpret_cast<const int4 *>(bias + c)) : make_int4(0, 0, 0, 0);
-      const int4 m4 =
-          in ? __ldg(reinterpret_cast<const int4 *>(rq.multiplier + c)) : make_int4(0, 0, 0, 0);
-      const int4 e4 =
-          in ? __ldg(reinterpret_cast<const int4 *>(rq.exponent + c)) : make_int4(0, 0, 0, 0);
-      bb[0] = b4.x, bb[1] = b4.y, bb[2] = b4.z, bb[3] = b4.w;
-      mm[0] = m4.x, mm[1] = m4.y, mm[2] = m4.z, mm[3] = m4.w;
-      ee[0] = e4.x, ee[1] = e4.y, ee[2] = e4.z, ee[3] = e4.w;
-    } else {
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const bool in = 4 * j + t < cols_left && c + t < K;
-        bb[t] = in ? __ldg(bias + c + t) : 0;
-        mm[t] = in ? __ldg(rq.multiplier + c + t) : 0;
-        ee[t] = in ? __ldg(rq.exponent + c + t) : 0;
-      }
-    }
     int32_t y[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t)
-      y[t] = rq_apply_dev(static_cast<int32_t>(v[4 * j + t] + static_cast<uint32_t>(bb[t])),
-                          rq_channel(mm[t], ee[t]), rq.zero_point, lo);
+    for (int t = 0; t < 4; ++t) y[t] = rq_apply_entry(v[4 * j + t], table[4 * j + t], zero_point, lo);
     w8[j] = rq_pack4(y[0], y[1], y[2], y[3]);
   }
 }
@@ -492,11 +469,14 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         PAIR ? mapa_shared(smem_u32(&tempty[1]), 0) : smem_u32(&tempty[1]);
     const int32_t lo = rq.relu ? rq.zero_point : -128;
     int8_t *out8 = reinterpret_cast<int8_t *>(out);
-    // Two 32-row x 32-byte staging buffers per warp (TMA store source).
+    // Per warp: one 32-row x 32-byte staging buffer (TMA store source) and
+    // the channel tables of its (at most two: BN <= 256) 32-column blocks,
+    // rebuilt only when the tile's N offset changes.
     uint8_t *stg_w = reinterpret_cast<uint8_t *>(staging) + (warp - 2) * 2048;
+    int4 *tables = reinterpret_cast<int4 *>(stg_w + 1024);
+    int table_n0 = -1;
     int acc = 0;
     uint32_t acc_phase = 0;
-    int ci = 0;
     for (int tile = tile_first; tile < g.num_tiles; tile += tile_step) {
       const int m_tile = tile / g.n_tiles;
       const int n_tile = tile - m_tile * g.n_tiles;
@@ -520,6 +500,19 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * g.acc_stride;
       const int row0 = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + quarter * 32;
+      if (n0 != table_n0) {
+        // Lane l fills entry l of each block's table (zero past BN or K).
+        __syncwarp();
+        for (int b = 0, c0 = 32 * cgroup; c0 < g.bn; ++b, c0 += 32 * kGroups) {
+          const int c = n0 + c0 + lane;
+          const bool in = c0 + lane < g.bn && c < g.K;
+          tables[b * 32 + lane] =
+              in ? rq_entry(__ldg(bias + c), __ldg(rq.multiplier + c), __ldg(rq.exponent + c))
+                 : make_int4(0, 0, 0, 0);
+        }
+        __syncwarp();
+        table_n0 = n0;
+      }
       bool released = false;
       auto release = [&] {
         tc_fence_before();
@@ -532,23 +525,24 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         }
         released = true;
       };
-      for (int c0 = 32 * cgroup; c0 < g.bn; c0 += 32 * kGroups) {
+      for (int b = 0, c0 = 32 * cgroup; c0 < g.bn; ++b, c0 += 32 * kGroups) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + c0, v);
         tmem_ld_wait();
         if (c0 + 32 * kGroups >= g.bn) release();  // this warp's last read of the tile
         const int col0 = n0 + c0;
         uint32_t w8[8];
-        requant_block(v, bias, rq, col0, g.bn - c0, g.K, lo, w8);
+        requant_block(v, tables + b * 32, rq.zero_point, lo, w8);
         const int4 lo16 = make_int4(static_cast<int32_t>(w8[0]), static_cast<int32_t>(w8[1]),
                                     static_cast<int32_t>(w8[2]), static_cast<int32_t>(w8[3]));
         const int4 hi16 = make_int4(static_cast<int32_t>(w8[4]), static_cast<int32_t>(w8[5]),
                                     static_cast<int32_t>(w8[6]), static_cast<int32_t>(w8[7]));
         if (g.tma_store) {
           // 32 rows x 32 bytes leave as one TMA store (columns >= K, rows >= M
-          // clipped); the buffer was read by the store two blocks ago.
-          int4 *stg = reinterpret_cast<int4 *>(stg_w + (ci & 1) * 1024);
-          if (lane == 0) bulk_wait_group_read<1>();
+          // clipped); the previous block's store has read the buffer by now
+          // (a whole block of arithmetic ago), the wait makes sure.
+          int4 *stg = reinterpret_cast<int4 *>(stg_w);
+          if (lane == 0) bulk_wait_group_read<0>();
           __syncwarp();
           stg[2 * lane] = lo16;
           stg[2 * lane + 1] = hi16;
@@ -558,7 +552,6 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
             tma_store_2d(&tmap_y, stg, col0, row0);
             bulk_commit_group();
           }
-          ++ci;
         } else if (valid && col0 < g.K) {
           if (rq.layout == 1) {
             // NCHW_VECT_C: the block is one 32-channel vector of this pixel

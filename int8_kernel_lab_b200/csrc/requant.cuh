@@ -96,15 +96,15 @@ __device__ __forceinline__ int32_t rq_apply_dev(int32_t t, const RqChannel &c, i
     const int64_t s = static_cast<int64_t>(t) * (int64_t(1) << c.left);
     t = s > INT32_MAX ? INT32_MAX : (s < INT32_MIN ? INT32_MIN : static_cast<int32_t>(s));
   }
+  // The doubling high multiply.  For ab = t * multiplier, the nudge-then-
+  // truncate form equals floor((ab + 2^30) / 2^31) for every ab (ab < 0,
+  // ab = -(k*2^31 + r): both give -k - [r > 2^30]), so one 64-bit add and an
+  // arithmetic shift suffice; only INT32_MIN * INT32_MIN saturates.
   int32_t v;
-  if (c.multiplier == INT32_MIN && t == INT32_MIN) {
+  if (c.multiplier == INT32_MIN && t == INT32_MIN)
     v = INT32_MAX;
-  } else {
-    const int64_t ab = static_cast<int64_t>(t) * c.multiplier;
-    const int64_t s = ab + (ab >= 0 ? (int64_t(1) << 30) : (int64_t(1) - (int64_t(1) << 30)));
-    // Truncating division by 2^31: bias negative values by 2^31 - 1 first.
-    v = static_cast<int32_t>((s + ((s >> 63) & ((int64_t(1) << 31) - 1))) >> 31);
-  }
+  else
+    v = static_cast<int32_t>((static_cast<int64_t>(t) * c.multiplier + (int64_t(1) << 30)) >> 31);
   if (c.right > 0) {
     const int32_t rem = v & c.mask;
     const int32_t threshold = (c.mask >> 1) + (v < 0 ? 1 : 0);
@@ -114,6 +114,46 @@ __device__ __forceinline__ int32_t rq_apply_dev(int32_t t, const RqChannel &c, i
   // final clamp makes the result the same.
   v = v < -4096 ? -4096 : (v > 4096 ? 4096 : v);
   v += zero_point;
+  v = v < lo ? lo : v;
+  return v > 127 ? 127 : v;
+}
+#endif
+
+#ifdef __CUDACC__
+// One channel's parameters as the int8 epilogue keeps them in shared memory:
+// {bias, multiplier, mask = 2^right - 1, right | left << 8 | slow << 16};
+// slow marks the rare channels that need rq_apply_dev's general path (a left
+// shift, or the INT32_MIN multiplier).
+__device__ __forceinline__ int4 rq_entry(int32_t bias, int32_t multiplier, int32_t exponent) {
+  const RqChannel c = rq_channel(multiplier, exponent);
+  const int32_t slow = (c.left > 0 || multiplier == INT32_MIN) ? 1 : 0;
+  return make_int4(bias, multiplier, c.mask, c.right | (c.left << 8) | (slow << 16));
+}
+
+__device__ __forceinline__ int32_t rq_sat_add(int32_t a, int32_t b) {
+  int32_t r;
+  asm("add.sat.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// rq_apply_dev on an accumulator and its channel's entry (bias not yet added).
+__device__ __forceinline__ int32_t rq_apply_entry(uint32_t acc, const int4 &e, int32_t zero_point,
+                                                  int32_t lo) {
+  const int32_t t = static_cast<int32_t>(acc + static_cast<uint32_t>(e.x));
+  if (e.w >> 16) {
+    RqChannel c;
+    c.multiplier = e.y;
+    c.right = e.w & 0xff;
+    c.left = (e.w >> 8) & 0xff;
+    c.mask = e.z;
+    return rq_apply_dev(t, c, zero_point, lo);
+  }
+  int32_t v = static_cast<int32_t>((static_cast<int64_t>(t) * e.y + (int64_t(1) << 30)) >> 31);
+  // Rounding divide by 2^right (right = 0: mask 0, v unchanged).
+  const int32_t rem = v & e.z;
+  const int32_t threshold = (e.z >> 1) + (v < 0 ? 1 : 0);
+  v = (v >> (e.w & 0xff)) + (rem > threshold ? 1 : 0);
+  v = rq_sat_add(v, zero_point);
   v = v < lo ? lo : v;
   return v > 127 ? 127 : v;
 }
