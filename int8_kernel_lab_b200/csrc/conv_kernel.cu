@@ -138,15 +138,29 @@ __device__ __forceinline__ void commit_to(uint64_t *bar) {
 // channel entries (rq_entry, bias included); every lane reads each entry with
 // one broadcast load.  `lo` is the lower clamp (the zero point with ReLU,
 // else -128).
+// `slow`: some channel of the block needs the general path (decided once per
+// block, so the common case is straight-line code).
 __device__ __forceinline__ void requant_block(const uint32_t (&v)[32], const int4 *table,
-                                              int32_t zero_point, int32_t lo,
+                                              int32_t zero_point, int32_t lo, bool slow,
                                               uint32_t (&w8)[8]) {
+  if (!slow) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    int32_t y[4];
+    for (int j = 0; j < 8; ++j) {
+      int32_t y[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) y[t] = rq_apply_entry(v[4 * j + t], table[4 * j + t], zero_point, lo);
-    w8[j] = rq_pack4(y[0], y[1], y[2], y[3]);
+      for (int t = 0; t < 4; ++t)
+        y[t] = rq_apply_fast(v[4 * j + t], table[4 * j + t], zero_point, lo);
+      w8[j] = rq_pack4(y[0], y[1], y[2], y[3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int32_t y[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        y[t] = rq_apply_entry(v[4 * j + t], table[4 * j + t], zero_point, lo);
+      w8[j] = rq_pack4(y[0], y[1], y[2], y[3]);
+    }
   }
 }
 
@@ -475,6 +489,7 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
     uint8_t *stg_w = reinterpret_cast<uint8_t *>(staging) + (warp - 2) * 2048;
     int4 *tables = reinterpret_cast<int4 *>(stg_w + 1024);
     int table_n0 = -1;
+    uint32_t slow_blocks = 0;  // bit b: block b has a slow-path channel
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = tile_first; tile < g.num_tiles; tile += tile_step) {
@@ -503,12 +518,15 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
       if (n0 != table_n0) {
         // Lane l fills entry l of each block's table (zero past BN or K).
         __syncwarp();
+        slow_blocks = 0;
         for (int b = 0, c0 = 32 * cgroup; c0 < g.bn; ++b, c0 += 32 * kGroups) {
           const int c = n0 + c0 + lane;
           const bool in = c0 + lane < g.bn && c < g.K;
-          tables[b * 32 + lane] =
+          const int4 e =
               in ? rq_entry(__ldg(bias + c), __ldg(rq.multiplier + c), __ldg(rq.exponent + c))
                  : make_int4(0, 0, 0, 0);
+          tables[b * 32 + lane] = e;
+          if (__any_sync(0xffffffffu, (e.w >> 16) != 0)) slow_blocks |= 1u << b;
         }
         __syncwarp();
         table_n0 = n0;
@@ -532,7 +550,7 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         if (c0 + 32 * kGroups >= g.bn) release();  // this warp's last read of the tile
         const int col0 = n0 + c0;
         uint32_t w8[8];
-        requant_block(v, tables + b * 32, rq.zero_point, lo, w8);
+        requant_block(v, tables + b * 32, rq.zero_point, lo, ((slow_blocks >> b) & 1u) != 0, w8);
         const int4 lo16 = make_int4(static_cast<int32_t>(w8[0]), static_cast<int32_t>(w8[1]),
                                     static_cast<int32_t>(w8[2]), static_cast<int32_t>(w8[3]));
         const int4 hi16 = make_int4(static_cast<int32_t>(w8[4]), static_cast<int32_t>(w8[5]),

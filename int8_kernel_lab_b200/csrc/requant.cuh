@@ -136,18 +136,12 @@ __device__ __forceinline__ int32_t rq_sat_add(int32_t a, int32_t b) {
   return r;
 }
 
-// rq_apply_dev on an accumulator and its channel's entry (bias not yet added).
-__device__ __forceinline__ int32_t rq_apply_entry(uint32_t acc, const int4 &e, int32_t zero_point,
-                                                  int32_t lo) {
+// rq_apply_dev on an accumulator and its channel's entry (bias not yet
+// added), for entries without the slow flag: straight-line code, so a block
+// of them interleaves freely.
+__device__ __forceinline__ int32_t rq_apply_fast(uint32_t acc, const int4 &e, int32_t zero_point,
+                                                 int32_t lo) {
   const int32_t t = static_cast<int32_t>(acc + static_cast<uint32_t>(e.x));
-  if (e.w >> 16) {
-    RqChannel c;
-    c.multiplier = e.y;
-    c.right = e.w & 0xff;
-    c.left = (e.w >> 8) & 0xff;
-    c.mask = e.z;
-    return rq_apply_dev(t, c, zero_point, lo);
-  }
   int32_t v = static_cast<int32_t>((static_cast<int64_t>(t) * e.y + (int64_t(1) << 30)) >> 31);
   // Rounding divide by 2^right (right = 0: mask 0, v unchanged).
   const int32_t rem = v & e.z;
@@ -156,6 +150,20 @@ __device__ __forceinline__ int32_t rq_apply_entry(uint32_t acc, const int4 &e, i
   v = rq_sat_add(v, zero_point);
   v = v < lo ? lo : v;
   return v > 127 ? 127 : v;
+}
+
+// Any entry: the general path for slow-flagged channels.
+__device__ __forceinline__ int32_t rq_apply_entry(uint32_t acc, const int4 &e, int32_t zero_point,
+                                                  int32_t lo) {
+  if (e.w >> 16) {
+    RqChannel c;
+    c.multiplier = e.y;
+    c.right = e.w & 0xff;
+    c.left = (e.w >> 8) & 0xff;
+    c.mask = e.z;
+    return rq_apply_dev(static_cast<int32_t>(acc + static_cast<uint32_t>(e.x)), c, zero_point, lo);
+  }
+  return rq_apply_fast(acc, e, zero_point, lo);
 }
 #endif
 
