@@ -1,6 +1,7 @@
 // abi.cu - the extern "C" boundary declared in include/int8conv.h.
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include <atomic>
 
@@ -18,6 +19,73 @@ extern std::atomic<int> g_pairing;
 namespace {
 
 bool aligned16(const void *p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Per-thread cache of launch plans.  A launch whose device, family, shape,
+// buffers, CTA pairing and epilogue match an earlier launch on this thread
+// replays that plan (kernel, grid, tensor maps, geometry) instead of planning
+// and encoding descriptors again.  Thread-local, so no locking; a plan only
+// depends on the key's fields (the tensor maps hold the buffer addresses).
+struct PlanKey {
+  int32_t device, strategy, pairing, out_kind;
+  int8conv_shape shape;
+  int32_t zero_point, relu;
+  const void *x, *w, *b, *y, *multiplier, *exponent;
+};
+struct PlanSlot {
+  PlanKey key;
+  i8c::LaunchPlan plan;
+  bool used = false;
+};
+constexpr int kPlanSlots = 32;
+thread_local PlanSlot t_plans[kPlanSlots];
+
+PlanKey plan_key(int strategy, const int8conv_shape &s, const void *x, const void *w,
+                 const void *b, const void *y, int out_kind, const int8conv_requant *rq) {
+  PlanKey k;
+  memset(&k, 0, sizeof(k));
+  k.device = i8c::device_info().device;
+  k.strategy = strategy;
+  k.pairing = i8c::pairing_mode();
+  k.out_kind = out_kind;
+  k.shape = s;
+  k.x = x;
+  k.w = w;
+  k.b = b;
+  k.y = y;
+  if (rq != nullptr) {
+    k.zero_point = rq->zero_point;
+    k.relu = rq->relu;
+    k.multiplier = rq->multiplier;
+    k.exponent = rq->exponent;
+  }
+  return k;
+}
+
+PlanSlot &plan_slot(const PlanKey &key) {
+  const uint64_t *p = reinterpret_cast<const uint64_t *>(&key);
+  uint64_t h = 0x9e3779b97f4a7c15ull;
+  for (size_t i = 0; i < sizeof(PlanKey) / 8; ++i) h = (h ^ p[i]) * 0x100000001b3ull;
+  return t_plans[(h >> 32) % kPlanSlots];
+}
+
+// Replays a cached plan, or runs `launch` (the family launcher) with plan
+// capture on and caches what it launched.
+template <class Launch>
+int8conv_status launch_cached(const PlanKey &key, cudaStream_t stream, Launch launch) {
+  PlanSlot &slot = plan_slot(key);
+  if (slot.used && memcmp(&slot.key, &key, sizeof(PlanKey)) == 0)
+    return i8c::launch_plan(slot.plan, stream);
+  i8c::LaunchPlan plan;
+  i8c::plan_capture_begin(&plan);
+  const int8conv_status st = launch();
+  i8c::plan_capture_end();
+  if (st == INT8CONV_OK && plan.func != nullptr) {
+    slot.key = key;
+    slot.plan = plan;
+    slot.used = true;
+  }
+  return st;
+}
 
 // The kernel families implemented in this build.  A family whose kernel is
 // not built reports every shape as ineligible.
@@ -40,18 +108,21 @@ int8conv_status launch_family(int strategy, const int8conv_shape *shape, const i
   const int8conv_status dev = i8c::check_device();
   if (dev != INT8CONV_OK) return dev;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (strategy) {
-    case INT8CONV_GENERIC:
-      return i8c::launch_generic_impl(*shape, input, filter, bias, output, st);
-    case INT8CONV_STRIP:
-      return i8c::launch_strip_impl(*shape, input, filter, bias, output, st);
-    case INT8CONV_HALO:
-      return i8c::launch_halo_impl(*shape, input, filter, bias, output, st);
-    case INT8CONV_SPLITK:
-      return i8c::launch_splitk_impl(*shape, input, filter, bias, output, st);
-    default:
-      return INT8CONV_NOT_ELIGIBLE;
-  }
+  const PlanKey key = plan_key(strategy, *shape, input, filter, bias, output, 0, nullptr);
+  return launch_cached(key, st, [&]() -> int8conv_status {
+    switch (strategy) {
+      case INT8CONV_GENERIC:
+        return i8c::launch_generic_impl(*shape, input, filter, bias, output, st);
+      case INT8CONV_STRIP:
+        return i8c::launch_strip_impl(*shape, input, filter, bias, output, st);
+      case INT8CONV_HALO:
+        return i8c::launch_halo_impl(*shape, input, filter, bias, output, st);
+      case INT8CONV_SPLITK:
+        return i8c::launch_splitk_impl(*shape, input, filter, bias, output, st);
+      default:
+        return INT8CONV_NOT_ELIGIBLE;
+    }
+  });
 }
 
 }  // namespace
@@ -211,9 +282,13 @@ int8conv_status int8conv_launch_requant(int strategy, const int8conv_shape *shap
   const i8c::Requant rq{requant->multiplier, requant->exponent, requant->zero_point,
                         requant->relu, requant->layout};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (strategy == INT8CONV_SPLITK)
-    return i8c::launch_splitk_requant(*shape, input, filter, bias, rq, output, st);
-  return i8c::launch_conv_requant(strategy, *shape, input, filter, bias, rq, output, st);
+  const PlanKey key =
+      plan_key(strategy, *shape, input, filter, bias, output, 1 + requant->layout, requant);
+  return launch_cached(key, st, [&]() -> int8conv_status {
+    if (strategy == INT8CONV_SPLITK)
+      return i8c::launch_splitk_requant(*shape, input, filter, bias, rq, output, st);
+    return i8c::launch_conv_requant(strategy, *shape, input, filter, bias, rq, output, st);
+  });
 }
 
 int8conv_status int8conv_launch_host(int strategy, const int8conv_shape *shape,

@@ -899,27 +899,16 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
       return INT8CONV_CUDA_ERROR;
     slot.store(kMaxSmem, std::memory_order_relaxed);
   }
-  const RunCtl ctl = run_ctl();
   const int ctas = PAIR ? 2 * (g.num_tiles < dev.sm_count / 2 ? g.num_tiles : dev.sm_count / 2)
                         : (g.num_tiles < dev.sm_count ? g.num_tiles : dev.sm_count);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ctas, 1, 1);
-  cfg.blockDim = dim3(kernel_threads<REQ>(), 1, 1);
-  cfg.dynamicSmemBytes = smem_bytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = 2;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = PAIR ? 2 : 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], g, b,
-                                             static_cast<int32_t *>(y), ctl, rq);
-  note_launch();
-  return err == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
+  LaunchPlan lp;
+  lp.func = reinterpret_cast<const void *>(kernel);
+  lp.grid = dim3(ctas, 1, 1);
+  lp.block = dim3(kernel_threads<REQ>(), 1, 1);
+  lp.smem = smem_bytes;
+  lp.cluster = PAIR ? 2 : 1;
+  plan_args(lp, maps[0], maps[1], maps[2], g, b, static_cast<int32_t *>(y), RunCtl{}, rq);
+  return launch_plan(lp, stream);
 }
 
 template <int MODE, bool PAIR, bool REQ>

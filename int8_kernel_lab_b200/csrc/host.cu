@@ -161,6 +161,40 @@ RunCtl run_ctl() {
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+namespace {
+thread_local LaunchPlan *t_capture = nullptr;
+}  // namespace
+
+void plan_capture_begin(LaunchPlan *out) { t_capture = out; }
+void plan_capture_end() { t_capture = nullptr; }
+
+int8conv_status launch_plan(LaunchPlan &plan, cudaStream_t stream) {
+  if (plan.ctl_arg >= 0) {
+    const RunCtl ctl = run_ctl();
+    memcpy(plan.blob + plan.offset[plan.ctl_arg], &ctl, sizeof(ctl));
+  }
+  if (t_capture != nullptr) *t_capture = plan;
+  void *args[12];
+  for (int i = 0; i < plan.nargs; ++i) args[i] = plan.blob + plan.offset[i];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = plan.grid;
+  cfg.blockDim = plan.block;
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = plan.cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = plan.cluster > 1 ? 2 : 1;
+  const cudaError_t err = cudaLaunchKernelExC(&cfg, plan.func, args);
+  note_launch();
+  return err == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
+}
+
 int pairing_mode() { return g_pairing.load(std::memory_order_relaxed); }
 
 bool ensure_smem_attr(const void *kernel, int bytes) {

@@ -6,6 +6,9 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
+
+#include <type_traits>
 
 #include "conv_common.h"
 #include "int8conv.h"
@@ -67,6 +70,49 @@ int8conv_status launch_conv_requant(int strategy, const int8conv_shape &s, const
 int8conv_status launch_splitk_requant(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                       const int32_t *b, const Requant &rq, int8_t *y,
                                       cudaStream_t stream);
+
+// A fully planned launch: kernel, grid, shared memory, cluster size and the
+// kernel's argument block (tensor maps, geometry, pointers), so a repeated
+// launch of the same shape on the same buffers skips planning and descriptor
+// encoding.  The run controls (status word, wait limit, starve hook) are
+// refreshed from the current settings at every launch.
+struct LaunchPlan {
+  const void *func = nullptr;
+  dim3 grid, block;
+  uint32_t smem = 0;
+  uint32_t cluster = 1;                 // thread-block cluster size (x)
+  int nargs = 0;
+  uint16_t offset[12] = {};             // argument k lives at blob + offset[k]
+  int ctl_arg = -1;                     // index of the RunCtl argument
+  alignas(64) unsigned char blob[768];  // argument values, kernel-parameter aligned
+};
+
+// Packs typed kernel arguments into plan->blob (their types must be the
+// kernel's parameter types, in order).
+template <class... Args>
+void plan_args(LaunchPlan &plan, const Args &...args) {
+  size_t at = 0;
+  plan.nargs = 0;
+  auto put = [&](const auto &a) {
+    using T = std::decay_t<decltype(a)>;
+    at = (at + alignof(T) - 1) / alignof(T) * alignof(T);
+    memcpy(plan.blob + at, &a, sizeof(T));
+    if (std::is_same<T, RunCtl>::value) plan.ctl_arg = plan.nargs;
+    plan.offset[plan.nargs++] = static_cast<uint16_t>(at);
+    at += sizeof(T);
+  };
+  (put(args), ...);
+}
+
+// Launches a plan on `stream` with programmatic stream serialisation (and the
+// plan's cluster size); records it for the calling thread's plan cache when a
+// capture is active.
+int8conv_status launch_plan(LaunchPlan &plan, cudaStream_t stream);
+
+// Plan capture around one family launch: the family launcher hands its plan
+// to launch_plan, which copies it to `*out` when capture is on for this thread.
+void plan_capture_begin(LaunchPlan *out);
+void plan_capture_end();
 
 // Family launchers (valid, eligible shape; pointers already checked).
 int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,

@@ -389,24 +389,14 @@ static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &
       return INT8CONV_CUDA_ERROR;
     slot.store(kMaxSmem, std::memory_order_relaxed);
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sg.g.num_tiles * sg.splits, 1, 1);
-  cfg.blockDim = dim3(kSplitThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = sg.splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], sg, b,
-                                             static_cast<int32_t *>(y), run_ctl(), rq);
-  note_launch();
-  return err == cudaSuccess ? INT8CONV_OK : INT8CONV_CUDA_ERROR;
+  LaunchPlan plan;
+  plan.func = reinterpret_cast<const void *>(kernel);
+  plan.grid = dim3(sg.g.num_tiles * sg.splits, 1, 1);
+  plan.block = dim3(kSplitThreads, 1, 1);
+  plan.smem = smem;
+  plan.cluster = sg.splits;
+  plan_args(plan, maps[0], maps[1], sg, b, static_cast<int32_t *>(y), RunCtl{}, rq);
+  return launch_plan(plan, stream);
 }
 
 // Resident clusters per cluster size on the current device, queried once

@@ -218,6 +218,42 @@ def test_device_wait_timeout_is_reported_and_context_survives(cuda, pairing):
     assert np.array_equal(dy.cpu().numpy(), pyoracle.conv(shape, x, w, b))
 
 
+@pytest.mark.parametrize("family", ["generic", "splitk"])
+def test_cached_plan_replays_and_follows_run_controls(cuda, family):
+    # A repeated launch (same shape, buffers, family, pairing) replays the
+    # thread's cached launch plan.  The replay must give the same integers,
+    # honour the starve hook and wait limit set since it was cached, and keep
+    # working after they are cleared.
+    torch = cuda
+    shape = m.load_workloads()["cfg4b_small_3x3"]
+    x, w, b = m.make_inputs(shape, seed=11)
+    dx, dw, db = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    dy = torch.zeros(shape.output_elements, dtype=torch.int32, device="cuda")
+    want = pyoracle.conv(shape, x, w, b)
+    for _ in range(3):
+        dy.zero_()
+        m.launch(family, shape, dx, dw, db, dy)
+        assert m.device_status() == _abi.OK
+        assert np.array_equal(dy.cpu().numpy(), want)
+    m.set_wait_limit_ns(20_000_000)
+    m.debug_starve_producer(True)
+    try:
+        m.launch(family, shape, dx, dw, db, dy)
+        assert m.device_status() == _abi.DEVICE_TIMEOUT
+    finally:
+        m.debug_starve_producer(False)
+        m.set_wait_limit_ns(0)
+    dy.zero_()
+    m.launch(family, shape, dx, dw, db, dy)
+    assert m.device_status() == _abi.OK
+    assert np.array_equal(dy.cpu().numpy(), want)
+    # Other buffers with the same shape: a different plan, not the cached one.
+    dy2 = torch.zeros_like(dy)
+    m.launch(family, shape, dx, dw, db, dy2)
+    assert m.device_status() == _abi.OK
+    assert np.array_equal(dy2.cpu().numpy(), want)
+
+
 @pytest.mark.parametrize("chunks", [1, 3, 64])
 def test_host_buffer_pipeline(cuda, chunks):
     # int8conv_launch_host: pinned host buffers in, host output back, with the
