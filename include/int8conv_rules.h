@@ -50,8 +50,9 @@ I8C_RULE int i8c_shape_valid(const int8conv_shape *s) {
          s->dilation_w <= 4096 &&
          /* conv_shape.cuh:34 */ s->c % 16 == 0 &&
          /* conv_shape.cuh:35 */ i8c_out_h(s) > 0 && i8c_out_w(s) > 0 &&
-         /* NHWK index and NHWC extent stay inside int64 and the kernels' int32 row index */
-         (int64_t)s->n * i8c_out_h(s) * i8c_out_w(s) < ((int64_t)1 << 31) &&
+         /* The kernels' int32 row index runs up to one 256-row tile past the
+          * last output row, and the NHWC pixel index stays inside int32. */
+         (int64_t)s->n * i8c_out_h(s) * i8c_out_w(s) < ((int64_t)1 << 31) - 512 &&
          (int64_t)s->n * s->h * s->w < ((int64_t)1 << 31);
 }
 

@@ -820,7 +820,7 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
     g.rows = halo ? out_h + (s.r - 1) * s.dilation_h : out_h;
     g.PWp = g.rows * g.Wp;
     positions = static_cast<int64_t>(s.n) * g.PWp;
-    if (positions >= (int64_t(1) << 31)) return false;
+    if (positions >= (int64_t(1) << 31) - 512) return false;  // int32 row index + one tile
     g.Mp = static_cast<int32_t>(positions);
     const int64_t shift = halo ? static_cast<int64_t>(s.r - 1) * s.dilation_h * g.Wp +
                                      static_cast<int64_t>(s.s - 1) * s.dilation_w

@@ -87,3 +87,13 @@ def test_select_returns_an_eligible_family():
     for name, s in m.load_workloads().items():
         fam = s.select()
         assert s.eligible(fam), name
+
+
+def test_row_count_bound_leaves_a_tile_of_slack():
+    # The kernels index rows as int32 and run up to one 256-row tile past the
+    # last row, so N*P*Q must stay below 2^31 - 512.
+    ok = m.ConvShape(1, 256, 8388605, 16, 16, 1, 1, 0, 0, 1, 1, 1, 1)
+    assert ok.n * ok.out_h * ok.out_w == 2**31 - 768 and ok.valid
+    for w in (8388606, 8388607):  # 2^31 - 512, 2^31 - 256 rows
+        big = m.ConvShape(1, 256, w, 16, 16, 1, 1, 0, 0, 1, 1, 1, 1)
+        assert big.n * big.h * big.w < 2**31 and not big.valid

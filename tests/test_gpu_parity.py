@@ -274,3 +274,28 @@ def test_host_buffer_pipeline(cuda, chunks):
     s.synchronize()
     assert m.device_status() == _abi.OK
     assert np.array_equal(hy.numpy(), pyoracle.conv(shape, x, w, b))
+
+
+def test_output_beyond_2g_elements(cuda):
+    # Maximum-size indexing: 2^21 output rows x 1040 channels = 2.18e9 int32
+    # outputs (8.7 GB), past 2^31 elements, with five 208-wide N tiles.  The
+    # first and last output rows and a seeded sample are checked.
+    torch = cuda
+    shape = m.ConvShape(2, 1024, 1024, 16, 1040, 3, 3, 1, 1, 1, 1, 1, 1)
+    assert shape.output_elements > (1 << 31)
+    x, w, b = m.make_inputs(shape, seed=17)
+    dx, dw, db = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    dy = torch.empty(shape.output_elements, dtype=torch.int32, device="cuda")
+    rng = np.random.RandomState(5)
+    rows = shape.n * shape.out_h * shape.out_w
+    idx = np.concatenate([np.arange(shape.k), (rows - 1) * shape.k + np.arange(shape.k),
+                          rng.randint(0, shape.output_elements, 100_000, dtype=np.int64)])
+    want = pyoracle.values(shape, x, w, b, idx)
+    for fam in ("generic", "auto"):
+        dy.fill_(-7)
+        m.launch(fam, shape, dx, dw, db, dy)
+        assert m.device_status() == _abi.OK
+        got = dy[torch.from_numpy(idx).cuda()].cpu().numpy()
+        assert np.array_equal(got, want), f"{fam}: {np.count_nonzero(got != want)} mismatches"
+    del dy
+    torch.cuda.empty_cache()
