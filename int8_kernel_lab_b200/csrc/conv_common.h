@@ -50,7 +50,6 @@ struct RunCtl {
 };
 
 constexpr int kBlockM = 128;         // MMA M (rows = output pixels)
-constexpr int kThreads = 192;        // 6 warps (GENERIC/STRIP/HALO kernels)
 constexpr int kSplitThreads = 192;   // 6 warps (SPLITK kernel)
 constexpr int kMaxSmem = 232448;     // 227 KB opt-in limit per block on sm_100
 

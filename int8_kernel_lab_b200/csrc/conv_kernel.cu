@@ -1,5 +1,5 @@
-// conv_kernel.cu - GENERIC and STRIP families: INT8 implicit-GEMM convolution
-// on tcgen05 tensor cores.
+// conv_kernel.cu - GENERIC, STRIP and HALO families: INT8 implicit-GEMM
+// convolution on tcgen05 tensor cores.
 //
 // Contract of the reference kernels it replaces (generic_implicit_gemm_kernel,
 // include/generic_implicit_gemm.cuh:90-153 / :170-227, and spatial_strip_kernel,
@@ -7,7 +7,7 @@
 //   out[m*K + k] = bias[k] + sum_{r,s,c} X[n, oy*sh + r*dh - ph, ox*sw + s*dw - pw, c] * W[k,r,s,c]
 // with padding taps contributing nothing (here: zero-filled by TMA).
 //
-// B200 design (persistent CTAs, 6 warps each):
+// B200 design (persistent CTAs, 6 warps each; 18 with the int8 epilogue):
 //   warp 0     TMA producer.  Activations come through an im2col tensor map
 //              (padding, stride and dilation are done by the TMA unit:
 //              bounding-box corners, traversal strides, per-tap offsets),
@@ -17,10 +17,17 @@
 //   warp 1     MMA issuer: tcgen05.mma kind::i8, K=32 bytes per instruction,
 //              int32 accumulators in TMEM.  Two accumulator buffers let the
 //              epilogue of tile i overlap the mainloop of tile i+1.
-//   warps 2-5  epilogue: tcgen05.ld (one output pixel row per thread), a
-//              transpose through swizzled shared memory, + bias, and streaming
-//              16-byte stores in which each warp instruction writes whole
-//              128-byte segments of four NHWK output rows.
+//   warps 2-5  epilogue: tcgen05.ld (one output pixel row per thread),
+//              + bias, a 32 x 32 int32 block staged in 128-byte-swizzled
+//              shared memory and written by one TMA tensor store (rows >= M
+//              and columns >= K clipped).  Where a TMA store does not apply
+//              (STRIP/HALO padded rows, K % 4 != 0, a block crossing into
+//              the next N tile) the staged block is transposed and leaves as
+//              16-byte stores that write whole 128-byte row segments.
+//   warps 2-17 with the requantised int8 epilogue (REQ): four warps per TMEM
+//              lane quarter, each owning every fourth 32-column block;
+//              per-N-tile channel tables in shared memory; 32 x 32-byte TMA
+//              stores (NHWC) or 32-byte vector stores (NCHW_VECT_C).
 //
 // Single CTA (PAIR = false): cta_group::1, M = 128 rows per tile.
 // CTA pair (PAIR = true, cluster of 2): cta_group::2, M = 256 rows per tile.
@@ -42,6 +49,10 @@
 //   computed and dropped by the epilogue.  The reference reused a 130-pixel
 //   strip across the 3 filter columns the same way (spatial_strip.cuh:17-29,
 //   :98-116), for out_w % 128 == 0 only.
+// HALO (unit strides): the M dimension runs over the zero-padded image
+//   (Hp x Wp positions per image); one staged tile of 128 + (R-1)*dh*Wp +
+//   (S-1)*dw positions per channel block feeds all R*S taps, tap (r, s)
+//   reading it r*dh*Wp + s*dw rows further on.
 // The reference's odd-K epilogue bug (generic_implicit_gemm.cuh:218-225) has
 // no counterpart: every column < K is stored.
 #include <cuda.h>
