@@ -611,7 +611,8 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         acc_phase ^= 1u;
       }
     }
-    if (g.tma_store && lane == 0) bulk_wait_group_all();
+    // Stores still reading shared memory finish before the CTA exits.
+    if (g.tma_store && lane == 0) bulk_wait_group_read_all();
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
@@ -624,6 +625,11 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         PAIR ? mapa_shared(smem_u32(&tempty[1]), 0) : smem_u32(&tempty[1]);
     int acc = 0;
     uint32_t acc_phase = 0;
+    // The first tile's bias lines come into L1 while the mainloop runs.
+    if (tile_first < g.num_tiles && lane < 8 && quarter == 0) {
+      const int c = (tile_first % g.n_tiles) * g.bn + 32 * lane;
+      if (32 * lane < g.bn && c < g.K) prefetch_l1(bias + c);
+    }
     // Staging buffers alternate by a block counter that runs across tiles, so
     // consecutive stores never share a buffer even when BN/32 is odd.
     int ci = 0;
@@ -744,8 +750,8 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         acc_phase ^= 1u;
       }
     }
-    // Output stores still reading shared memory or in flight finish first.
-    if (g.tma_store && lane == 0) bulk_wait_group_all();
+    // Stores still reading shared memory finish before the CTA exits.
+    if (g.tma_store && lane == 0) bulk_wait_group_read_all();
   }
 
   tc_fence_before();

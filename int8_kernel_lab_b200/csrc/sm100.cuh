@@ -165,6 +165,19 @@ __device__ __forceinline__ void bulk_wait_group_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// Waits until every committed store group has finished reading shared
+// memory: what a CTA must wait for before it exits (its shared memory goes
+// away); the global writes complete with the grid, before any later kernel
+// in the stream (or a dependent launch past griddepcontrol.wait) runs.
+__device__ __forceinline__ void bulk_wait_group_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Prefetches the 128-byte line holding `p` into L1.
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 // ---- tcgen05 ----------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
