@@ -299,3 +299,30 @@ def test_output_beyond_2g_elements(cuda):
         assert np.array_equal(got, want), f"{fam}: {np.count_nonzero(got != want)} mismatches"
     del dy
     torch.cuda.empty_cache()
+
+
+GUARD_BYTES = 4096
+
+
+@pytest.mark.parametrize("name", ["cfg4c_tail_k100", "nonmultiple8_k63", "cfg1_smoke", "k288",
+                                  "cfg2_n3"])
+def test_no_writes_outside_the_output(cuda, pairing, name):
+    # Stand-in for a sanitizer (closed on this pool): the output sits between
+    # two poisoned 4 KB guard bands, and no family may touch them.
+    torch = cuda
+    table = m.load_workloads()
+    shape = {"k288": m.ConvShape(2, 14, 14, 64, 288, 3, 3, 1, 1, 1, 1, 1, 1),
+             "cfg2_n3": table["cfg2_mid_3x3"].with_batch(3)}.get(name) or table[name]
+    x, w, b = m.make_inputs(shape, seed=29)
+    dx, dw, db = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    g = GUARD_BYTES // 4
+    want = pyoracle.conv(shape, x, w, b)
+    for fam in _families(shape):
+        buf = torch.full((shape.output_elements + 2 * g,), 0x5A5A5A5A, dtype=torch.int32,
+                         device="cuda")
+        m.launch(fam, shape, dx, dw, db, buf[g:g + shape.output_elements])
+        assert m.device_status() == _abi.OK
+        host = buf.cpu().numpy()
+        assert np.all(host[:g] == 0x5A5A5A5A), f"{fam} wrote before the output"
+        assert np.all(host[g + shape.output_elements:] == 0x5A5A5A5A), f"{fam} wrote past it"
+        assert np.array_equal(host[g:g + shape.output_elements], want), fam
