@@ -132,6 +132,51 @@ def test_reference_workloads(cuda, name):
             _sampled_check(shape, x, w, b, got, samples=50_000, whole_images=(0,))
 
 
+def _random_wide_shapes(count, seed=77):
+    """Wider parameters: pads to 7, strides to 8, dilations to 6, taps to
+    11 x 11, C to 512, K to 700 (kept to oracle-friendly sizes)."""
+    rng = np.random.RandomState(seed)
+    out = []
+    while len(out) < count:
+        sh = m.ConvShape(
+            n=int(rng.randint(1, 3)), h=int(rng.randint(4, 48)), w=int(rng.randint(4, 48)),
+            c=int(16 * rng.randint(1, 33)), k=int(rng.randint(1, 701)),
+            r=int(rng.randint(1, 12)), s=int(rng.randint(1, 12)),
+            pad_h=int(rng.randint(0, 8)), pad_w=int(rng.randint(0, 8)),
+            stride_h=int(rng.randint(1, 9)), stride_w=int(rng.randint(1, 9)),
+            dilation_h=int(rng.randint(1, 7)), dilation_w=int(rng.randint(1, 7)))
+        if sh.valid and sh.eligible("generic") and sh.ops <= 4e9:
+            out.append(sh)
+    return out
+
+
+WIDE_SHAPES = _random_wide_shapes(24)
+
+
+@pytest.mark.parametrize("idx", range(len(WIDE_SHAPES)))
+def test_random_wide_shapes(cuda, idx):
+    shape = WIDE_SHAPES[idx]
+    x, w, b = m.make_inputs(shape, seed=100 + idx)
+    want = pyoracle.conv(shape, x, w, b)
+    for fam in _families(shape):
+        got = _run(cuda, fam, shape, x, w, b)
+        bad = np.count_nonzero(got != want)
+        assert bad == 0, f"{fam} on {shape}: {bad} mismatches"
+    # The int8 epilogue on the same shape, in each layout it allows.
+    rng = np.random.RandomState(idx)
+    mult = rng.randint(1 << 30, (1 << 31) - 1, shape.k, dtype=np.int64).astype(np.int32)
+    expo = rng.randint(-14, -4, shape.k).astype(np.int32)
+    dev = [cuda.from_numpy(a).cuda() for a in (x, w, b, mult, expo)]
+    for layout in ["nhwc"] + (["nchw_vect_c"] if shape.k % 32 == 0 else []):
+        y8 = cuda.zeros(shape.output_elements, dtype=cuda.int8, device="cuda")
+        m.launch_requant("auto", shape, *dev, y8, zero_point=4, relu=True, layout=layout)
+        assert m.device_status() == _abi.OK
+        want8 = pyoracle.requant(want, shape.k, mult, expo, zero_point=4, relu=True)
+        if layout == "nchw_vect_c":
+            want8 = pyoracle.to_nchw_vect_c(want8, shape.n, shape.out_h, shape.out_w, shape.k)
+        assert np.array_equal(y8.cpu().numpy(), want8), f"requant {layout} on {shape}"
+
+
 def _random_shapes(count, seed=2026):
     rng = np.random.RandomState(seed)
     out = []
