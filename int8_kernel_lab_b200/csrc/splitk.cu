@@ -243,13 +243,21 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     const int col = n0 + 4 * cg;
     if (m >= g.M || col >= g.K) continue;
     const uint32_t off = part_base + rr * sg.part_pitch + cg * 16;
+    // Every split's load is issued before any is summed, so the remote
+    // latencies overlap instead of adding up.
+    int4 part[kMaxSplits];
+#pragma unroll
+    for (int p = 0; p < kMaxSplits; ++p)
+      if (p < sg.splits) part[p] = ld_cluster_v4(mapa_shared(off, static_cast<uint32_t>(p)));
     int4 acc = make_int4(0, 0, 0, 0);
-    for (int p = 0; p < sg.splits; ++p) {
-      const int4 v = ld_cluster_v4(mapa_shared(off, static_cast<uint32_t>(p)));
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+#pragma unroll
+    for (int p = 0; p < kMaxSplits; ++p) {
+      if (p < sg.splits) {
+        acc.x += part[p].x;
+        acc.y += part[p].y;
+        acc.z += part[p].z;
+        acc.w += part[p].w;
+      }
     }
     if constexpr (REQ) {
       // Four int8 outputs of one row: NHWC bytes m*K + col.., or one quarter
