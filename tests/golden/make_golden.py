@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Generates tests/golden/*.npz from the reference's OWN CPU oracle.
 
-Run here, where the reference sources exist (they are not on the GPU box):
-    python tests/golden/make_golden.py [--reference /root/reference]
+Run where the reference sources exist (the GPU box has none):
+    python tests/golden/make_golden.py [--reference PATH_TO_INT8_KERNEL_LAB]
 
 For every row of golden_cases.csv it builds oracle/_ref/ref_<case> with
 oracle/Makefile (the reference's src/conv_lab.cu compiled unchanged, its
