@@ -56,6 +56,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the workload's batch N (a measurement aid: one GPU "
+                         "running N/G images reproduces one rank of a G-GPU job)")
     ap.add_argument("--strategy", default="auto")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--e2e-chunks", type=int, default=8,
@@ -245,6 +248,8 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
 
     full = m.load_workloads()[args.workload]
+    if args.batch > 0:
+        full = full.with_batch(args.batch)
     lo, hi = shard(full.n, rank, world)
     local_shape = full.with_batch(hi - lo)
     x, w, b = m.make_inputs(full)

@@ -30,6 +30,11 @@ struct ConvGeom {
   int32_t tma_store; // 1: epilogue writes 32x32 blocks with TMA tensor stores
   int32_t stages;    // shared-memory ring depth (B ring; also A for GENERIC)
   int32_t m_tiles, n_tiles, num_tiles;
+  // Tail balancing: tiles [split_from, num_tiles) (the last, partial wave)
+  // are each cut into split_f column parts of bn / split_f, so that wave
+  // finishes sooner; work units are the whole tiles before split_from, then
+  // the parts.  split_f = 1 and num_units = num_tiles when nothing is cut.
+  int32_t split_from, split_f, num_units;
   // STRIP / HALO: the M dimension runs over padded-grid positions
   // (n, i, j), j in [0, Wp), i in [0, rows); positions with j >= out_w or
   // i >= out_h are computed and discarded.

@@ -136,6 +136,29 @@ struct Ring {
   }
 };
 
+// One work unit of the persistent schedule: a whole tile, or one column part
+// of a tile of the last wave (see ConvGeom::split_f).
+struct Unit {
+  int m_tile;  // 128- or 256-row tile index
+  int n0;      // first output channel of the unit
+  int bn;      // output channels of the unit
+};
+
+__device__ __forceinline__ Unit unit_at(const ConvGeom &g, int u) {
+  int tile = u, part = 0, bn = g.bn;
+  if (u >= g.split_from) {
+    const int idx = u - g.split_from;
+    tile = g.split_from + idx / g.split_f;
+    part = idx - (idx / g.split_f) * g.split_f;
+    bn = g.bn / g.split_f;
+  }
+  Unit t;
+  t.m_tile = tile / g.n_tiles;
+  t.n0 = (tile - t.m_tile * g.n_tiles) * g.bn + part * bn;
+  t.bn = bn;
+  return t;
+}
+
 template <bool PAIR>
 __device__ __forceinline__ void commit_to(uint64_t *bar) {
   if constexpr (PAIR)
@@ -283,11 +306,13 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         return PAIR ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar);
       };
       bool ok = true;
-      for (int tile = tile_first; tile < g.num_tiles && ok; tile += tile_step) {
-        const int m_tile = tile / g.n_tiles;
-        const int n_tile = tile - m_tile * g.n_tiles;
+      for (int tile = tile_first; tile < g.num_units && ok; tile += tile_step) {
+        const Unit t = unit_at(g, tile);
+        const int m_tile = t.m_tile;
         const int m0 = m_tile * kTileRows + static_cast<int>(rank) * kBlockM;
-        const int n0 = n_tile * g.bn + static_cast<int>(rank) * b_rows;
+        // Each CTA of a pair loads its half of the unit's filter rows (a box
+        // of b_rows; a split unit uses the first bn/2 of them).
+        const int n0 = t.n0 + static_cast<int>(rank) * (PAIR ? t.bn / 2 : 0);
         const int img = m0 / m_span;
         const int rem = m0 - img * m_span;
         const int p = rem / m_row;
@@ -396,20 +421,23 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- MMA issuer (the leader of a pair) ----------------
-      const uint32_t idesc = idesc_s8(kTileRows, g.bn);
+      const uint32_t idesc_full = idesc_s8(kTileRows, g.bn);
+      const uint32_t idesc_part = idesc_s8(kTileRows, g.bn / g.split_f);
       constexpr Layout kLayout = SwizzleOf<CBLK>::kLayout;
       constexpr uint32_t kAtom = 8 * CBLK;  // 8 rows x CBLK bytes
       Ring ra, rb;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      uint32_t idesc = idesc_full;
       auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t accumulate) {
         if constexpr (PAIR)
           umma_i8_pair(d, a, b, idesc, accumulate);
         else
           umma_i8(d, a, b, idesc, accumulate);
       };
-      for (int tile = tile_first; tile < g.num_tiles && ok; tile += tile_step) {
+      for (int tile = tile_first; tile < g.num_units && ok; tile += tile_step) {
+        idesc = tile >= g.split_from ? idesc_part : idesc_full;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, wctx, kStatusTimeoutDrain)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * g.acc_stride);
@@ -499,15 +527,16 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
     // rebuilt only when the tile's N offset changes.
     uint8_t *stg_w = reinterpret_cast<uint8_t *>(staging) + (warp - 2) * 2048;
     int4 *tables = reinterpret_cast<int4 *>(stg_w + 1024);
-    int table_n0 = -1;
+    int table_n0 = -1, table_bn = 0;
     uint32_t slow_blocks = 0;  // bit b: block b has a slow-path channel
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = tile_first; tile < g.num_tiles; tile += tile_step) {
-      const int m_tile = tile / g.n_tiles;
-      const int n_tile = tile - m_tile * g.n_tiles;
+    for (int tile = tile_first; tile < g.num_units; tile += tile_step) {
+      const Unit t = unit_at(g, tile);
+      const int m_tile = t.m_tile;
       const int pos = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + row;
-      const int n0 = n_tile * g.bn;
+      const int n0 = t.n0;
+      const int bn = t.bn;
       bool valid = pos < m_limit;
       int m = pos;
       if constexpr (SHIFT) {
@@ -526,13 +555,13 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * g.acc_stride;
       const int row0 = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + quarter * 32;
-      if (n0 != table_n0) {
+      if (n0 != table_n0 || bn != table_bn) {
         // Lane l fills entry l of each block's table (zero past BN or K).
         __syncwarp();
         slow_blocks = 0;
-        for (int b = 0, c0 = 32 * cgroup; c0 < g.bn; ++b, c0 += 32 * kGroups) {
+        for (int b = 0, c0 = 32 * cgroup; c0 < bn; ++b, c0 += 32 * kGroups) {
           const int c = n0 + c0 + lane;
-          const bool in = c0 + lane < g.bn && c < g.K;
+          const bool in = c0 + lane < bn && c < g.K;
           const int4 e =
               in ? rq_entry(__ldg(bias + c), __ldg(rq.multiplier + c), __ldg(rq.exponent + c))
                  : make_int4(0, 0, 0, 0);
@@ -541,6 +570,7 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         }
         __syncwarp();
         table_n0 = n0;
+        table_bn = bn;
       }
       bool released = false;
       auto release = [&] {
@@ -554,11 +584,11 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         }
         released = true;
       };
-      for (int b = 0, c0 = 32 * cgroup; c0 < g.bn; ++b, c0 += 32 * kGroups) {
+      for (int b = 0, c0 = 32 * cgroup; c0 < bn; ++b, c0 += 32 * kGroups) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + c0, v);
         tmem_ld_wait();
-        if (c0 + 32 * kGroups >= g.bn) release();  // this warp's last read of the tile
+        if (c0 + 32 * kGroups >= bn) release();  // this warp's last read of the tile
         const int col0 = n0 + c0;
         uint32_t w8[8];
         requant_block(v, tables + b * 32, rq.zero_point, lo, ((slow_blocks >> b) & 1u) != 0, w8);
@@ -593,7 +623,7 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
             __stcs(dst + 1, hi16);
           } else {
             int8_t *dst = out8 + static_cast<int64_t>(m) * g.K + col0;
-            const int span = g.bn - c0 < g.K - col0 ? g.bn - c0 : g.K - col0;
+            const int span = bn - c0 < g.K - col0 ? bn - c0 : g.K - col0;
             if (span >= 32 && (g.K & 15) == 0) {
               __stcs(reinterpret_cast<int4 *>(dst), lo16);
               __stcs(reinterpret_cast<int4 *>(dst) + 1, hi16);
@@ -626,18 +656,20 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     // The first tile's bias lines come into L1 while the mainloop runs.
-    if (tile_first < g.num_tiles && lane < 8 && quarter == 0) {
-      const int c = (tile_first % g.n_tiles) * g.bn + 32 * lane;
-      if (32 * lane < g.bn && c < g.K) prefetch_l1(bias + c);
+    if (tile_first < g.num_units && lane < 8 && quarter == 0) {
+      const Unit t = unit_at(g, tile_first);
+      const int c = t.n0 + 32 * lane;
+      if (32 * lane < t.bn && c < g.K) prefetch_l1(bias + c);
     }
     // Staging buffers alternate by a block counter that runs across tiles, so
     // consecutive stores never share a buffer even when BN/32 is odd.
     int ci = 0;
-    for (int tile = tile_first; tile < g.num_tiles; tile += tile_step) {
-      const int m_tile = tile / g.n_tiles;
-      const int n_tile = tile - m_tile * g.n_tiles;
+    for (int tile = tile_first; tile < g.num_units; tile += tile_step) {
+      const Unit t = unit_at(g, tile);
+      const int m_tile = t.m_tile;
       const int pos = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + row;
-      const int n0 = n_tile * g.bn;
+      const int n0 = t.n0;
+      const int bn = t.bn;
       bool valid = pos < m_limit;
       int m = pos;
       if constexpr (SHIFT) {
@@ -666,11 +698,11 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
       const int q = lane & 7;    // 16-byte column group this lane stores
       const int rsub = lane >> 3;
       const int row0 = m_tile * kTileRows + static_cast<int>(rank) * kBlockM + quarter * 32;
-      for (int c0 = 0; c0 < g.bn; c0 += 32) {
+      for (int c0 = 0; c0 < bn; c0 += 32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + c0, v);
         tmem_ld_wait();
-        if (c0 + 32 >= g.bn) {
+        if (c0 + 32 >= bn) {
           // Last read of this accumulator: hand it back to the MMA issuer now.
           tc_fence_before();
           __syncwarp();
@@ -689,7 +721,7 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const bool in = c0 + 4 * j < g.bn && col0 + 4 * j < g.K;
+            const bool in = c0 + 4 * j < bn && col0 + 4 * j < g.K;
             const int4 bb =
                 in ? __ldg(reinterpret_cast<const int4 *>(bias + col0) + j) : make_int4(0, 0, 0, 0);
             stg[lane * 8 + (j ^ (lane & 7))] = make_int4(
@@ -714,7 +746,7 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
         __syncwarp();
         if (vec_k) {
           // K % 4 == 0: 16-byte groups are wholly inside or outside [0, K).
-          const bool col_ok = c0 + 4 * q < g.bn && col0 + 4 * q < g.K;
+          const bool col_ok = c0 + 4 * q < bn && col0 + 4 * q < g.K;
           const int4 bb = col_ok ? __ldg(reinterpret_cast<const int4 *>(bias + col0) + q)
                                  : make_int4(0, 0, 0, 0);
 #pragma unroll
@@ -732,7 +764,7 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
             }
           }
         } else {
-          const bool col_ok = c0 + lane < g.bn && col0 + lane < g.K;
+          const bool col_ok = c0 + lane < bn && col0 + lane < g.K;
           const int32_t bl = col_ok ? __ldg(bias + col0 + lane) : 0;
           const int32_t *stg32 = reinterpret_cast<const int32_t *>(stg);
           for (int r = 0; r < 32; ++r) {
@@ -797,8 +829,9 @@ static int next_pow2(int v) {
 }
 
 // Fills the launch geometry; false if the shape does not fit the kernel.
-static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_kind, ConvGeom &g,
-                          int &cblk) {
+// `slots` = tiles the grid runs at once (CTA pairs or single CTAs).
+static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_kind, int slots,
+                          ConvGeom &g, int &cblk) {
   const int32_t out_h = (s.h + 2 * s.pad_h - s.dilation_h * (s.r - 1) - 1) / s.stride_h + 1;
   const int32_t out_w = (s.w + 2 * s.pad_w - s.dilation_w * (s.s - 1) - 1) / s.stride_w + 1;
   cblk = pick_cblk(s.c);
@@ -869,6 +902,33 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   g.m_tiles = static_cast<int32_t>((positions + tile_rows - 1) / tile_rows);
   g.n_tiles = (s.k + g.bn - 1) / g.bn;
   g.num_tiles = g.m_tiles * g.n_tiles;
+  // Tail balancing: the persistent grid runs `slots` tiles at once, so the
+  // last wave is partial when num_tiles % slots != 0.  Cutting each tile of
+  // that wave into f column parts (N = bn/f, still 32-column aligned for the
+  // stores) lets it finish in ceil(f*rem/slots)/f of a tile time instead of
+  // a whole one; pick the f (1, 2 or 4) with the shortest span.
+  g.split_from = g.num_tiles;
+  g.split_f = 1;
+  g.num_units = g.num_tiles;
+  if (slots > 0) {
+    const int waves = g.num_tiles / slots;
+    const int rem = g.num_tiles - waves * slots;
+    int best_f = 1;
+    int best_quarters = 4 * waves + (rem > 0 ? 4 : 0);  // span in quarter-tile units
+    for (int f = 2; f <= 4 && rem > 0; f *= 2) {
+      if (g.bn % (32 * f) != 0) continue;
+      const int span = 4 * waves + (4 / f) * ((f * rem + slots - 1) / slots);
+      if (span < best_quarters) {
+        best_quarters = span;
+        best_f = f;
+      }
+    }
+    if (best_f > 1) {
+      g.split_f = best_f;
+      g.split_from = g.num_tiles - rem;
+      g.num_units = g.split_from + best_f * rem;
+    }
+  }
   // TMA output stores: GENERIC rows are contiguous in NHWK; the row pitch
   // 4*K must be a multiple of 16 bytes; a 32-column block must not reach into
   // the next N tile (columns >= K are clipped, columns of a neighbour are not).
@@ -916,8 +976,8 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
       return INT8CONV_CUDA_ERROR;
     slot.store(kMaxSmem, std::memory_order_relaxed);
   }
-  const int ctas = PAIR ? 2 * (g.num_tiles < dev.sm_count / 2 ? g.num_tiles : dev.sm_count / 2)
-                        : (g.num_tiles < dev.sm_count ? g.num_tiles : dev.sm_count);
+  const int ctas = PAIR ? 2 * (g.num_units < dev.sm_count / 2 ? g.num_units : dev.sm_count / 2)
+                        : (g.num_units < dev.sm_count ? g.num_units : dev.sm_count);
   LaunchPlan lp;
   lp.func = reinterpret_cast<const void *>(kernel);
   lp.grid = dim3(ctas, 1, 1);
@@ -954,7 +1014,7 @@ static bool use_pair(const int8conv_shape &s, int mode, int out_kind) {
   if (pairing == 1) return false;
   ConvGeom g;
   int cblk = 0;
-  if (!plan_geometry(s, mode, true, out_kind, g, cblk)) return false;
+  if (!plan_geometry(s, mode, true, out_kind, device_info().sm_count / 2, g, cblk)) return false;
   if (pairing == 2) return true;
   const int64_t reduction = static_cast<int64_t>(s.r) * s.s * s.c;
   return g.bn == 256 && g.num_tiles >= device_info().sm_count &&
@@ -967,11 +1027,12 @@ static int8conv_status launch_mode(const int8conv_shape &s, const int8_t *x, con
                                    cudaStream_t stream) {
   ConvGeom g;
   int cblk = 0;
+  const int sms = device_info().sm_count;
   if (use_pair(s, MODE, out_kind)) {
-    if (!plan_geometry(s, MODE, true, out_kind, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+    if (!plan_geometry(s, MODE, true, out_kind, sms / 2, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
     return launch_cblk<MODE, true, REQ>(s, g, cblk, x, w, b, y, rq, stream);
   }
-  if (!plan_geometry(s, MODE, false, out_kind, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+  if (!plan_geometry(s, MODE, false, out_kind, sms, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
   return launch_cblk<MODE, false, REQ>(s, g, cblk, x, w, b, y, rq, stream);
 }
 
