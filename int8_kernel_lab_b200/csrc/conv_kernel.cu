@@ -905,8 +905,10 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   // Tail balancing: the persistent grid runs `slots` tiles at once, so the
   // last wave is partial when num_tiles % slots != 0.  Cutting each tile of
   // that wave into f column parts (N = bn/f, still 32-column aligned for the
-  // stores) lets it finish in ceil(f*rem/slots)/f of a tile time instead of
-  // a whole one; pick the f (1, 2 or 4) with the shortest span.
+  // stores) spreads it over more slots.  A part still loads its tile's whole
+  // activation block and filter box, so it costs about 1/f + 0.2 of a tile
+  // (B200 sweep of all 51 workloads: parts in several waves, e.g. 98 tiles
+  // on 148 CTAs as 392 quarters, were slower).  Spans are in 1/20 tile.
   g.split_from = g.num_tiles;
   g.split_f = 1;
   g.num_units = g.num_tiles;
@@ -914,12 +916,12 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
     const int waves = g.num_tiles / slots;
     const int rem = g.num_tiles - waves * slots;
     int best_f = 1;
-    int best_quarters = 4 * waves + (rem > 0 ? 4 : 0);  // span in quarter-tile units
+    int best_span = 20 * waves + (rem > 0 ? 20 : 0);
     for (int f = 2; f <= 4 && rem > 0; f *= 2) {
       if (g.bn % (32 * f) != 0) continue;
-      const int span = 4 * waves + (4 / f) * ((f * rem + slots - 1) / slots);
-      if (span < best_quarters) {
-        best_quarters = span;
+      const int span = 20 * waves + ((f * rem + slots - 1) / slots) * (20 / f + 4);
+      if (span < best_span) {
+        best_span = span;
         best_f = f;
       }
     }
