@@ -91,16 +91,19 @@ I8C_RULE int i8c_strip_eligible(const int8conv_shape *s) {
 
 /* Channel block (bytes of C per k-block, one swizzle width: 128, 64 or 32)
  * the kernels use for a shape.  Each k-block costs its CBLK bytes of MMA work
- * plus a fixed pipeline round trip worth about 64 bytes; channels past C in
- * the last block are zero-filled by TMA.  The cheapest block wins, ties going
- * to the one with less zero padding (C = 48 -> 64, C = 96 -> 128,
- * C = 192 -> 64, C % 128 == 0 -> 128). */
+ * plus a fixed cost worth about 128 bytes (a pipeline round trip and one
+ * im2col request per pixel); channels past C in the last block are
+ * zero-filled by TMA.  The cheapest block wins, ties going to the one with
+ * less zero padding (C = 48 -> 64, C = 96 -> 128, C = 160 or 192 -> 128,
+ * C % 128 == 0 -> 128).  Measured on B200 for C = 192 (BASELINE 5c): two
+ * 128-byte blocks, one of them half padding, beat three 64-byte blocks
+ * (36.4 vs 38.8 us per launch). */
 I8C_RULE int32_t i8c_channel_block(int32_t c) {
   int32_t best = 32;
   int64_t best_cost = -1, best_pad = 0;
   for (int32_t cb = 128; cb >= 32; cb /= 2) {
     const int64_t blocks = (c + cb - 1) / cb;
-    const int64_t cost = blocks * (cb + 64);
+    const int64_t cost = blocks * (cb + 128);
     const int64_t pad = blocks * cb - c;
     if (best_cost < 0 || cost < best_cost || (cost == best_cost && pad < best_pad)) {
       best = cb;

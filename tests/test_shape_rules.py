@@ -1,7 +1,11 @@
 """Eligibility predicates and the workloads table (host only)."""
+from pathlib import Path
+
 import pytest
 
 import int8_kernel_lab_b200 as m
+
+ROOT = Path(__file__).resolve().parent.parent
 
 
 def reference_strip_predicate(s):
@@ -84,3 +88,25 @@ def test_dispatch_needs_a_single_wave_split():
     assert table["batch8_3x3"].select() == "generic"
     for name in ("darknet_down_52", "cfg4a_deep_1x1", "darknet_head_13", "resnet_s4_3x3"):
         assert table[name].select() == "splitk", name
+
+
+def test_channel_block_choices(tmp_path):
+    # The k-block width each C gets (int8conv_rules.h, i8c_channel_block):
+    # cheapest blocks x (width + 128-byte fixed cost), ties to less padding.
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no gcc")
+    src = tmp_path / "cb.c"
+    src.write_text('#include <stdio.h>\n#include "int8conv_rules.h"\n'
+                   'int main(void){int cs[]={16,32,48,64,80,96,128,160,192,256,320,512};'
+                   'for(int i=0;i<12;++i) printf("%d %d\\n", cs[i], i8c_channel_block(cs[i]));'
+                   'return 0;}\n')
+    exe = tmp_path / "cb"
+    subprocess.run([gcc, "-std=c99", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)],
+                   check=True)
+    got = dict(tuple(map(int, line.split())) for line in
+               subprocess.run([str(exe)], capture_output=True, text=True).stdout.split("\n") if line)
+    assert got == {16: 32, 32: 32, 48: 64, 64: 64, 80: 128, 96: 128, 128: 128, 160: 128,
+                   192: 128, 256: 128, 320: 128, 512: 128}
