@@ -60,7 +60,7 @@ typedef enum int8conv_status {
 } int8conv_status;
 
 /* Kernel families.  GENERIC and STRIP mirror launch_generic / launch_spatial_strip
- * (include/generic_implicit_gemm.cuh:155-165, include/spatial_strip.cuh:528-540);
+ * (include/generic_implicit_gemm.cuh:155-165, include/spatial_strip.cuh:289-301);
  * HALO and SPLITK have no counterpart in the reference. */
 typedef enum int8conv_strategy {
   INT8CONV_GENERIC = 0,
@@ -115,7 +115,7 @@ int8conv_status int8conv_launch_generic(const int8conv_shape *shape,
                                         const int32_t *bias, int32_t *output,
                                         void *stream);
 
-/* launch_spatial_strip<Shape>(...) (include/spatial_strip.cuh:528-540). */
+/* launch_spatial_strip<Shape>(...) (include/spatial_strip.cuh:289-301). */
 int8conv_status int8conv_launch_spatial_strip(const int8conv_shape *shape,
                                               const int8_t *input, const int8_t *filter,
                                               const int32_t *bias, int32_t *output,

@@ -8,7 +8,7 @@
 //   launch_generic<Shape>(input, filter, bias, output, stream);            // generic_implicit_gemm.cuh:155-165
 //   launch_generic_sm80<Shape>(input, filter, bias, output, stream);       // generic_implicit_gemm.cuh:229-238
 //   if constexpr (kSpatialStripEligible<Shape>)                            // spatial_strip.cuh:11-15
-//     launch_spatial_strip<Shape>(input, filter, bias, output, stream);   // spatial_strip.cuh:528-540
+//     launch_spatial_strip<Shape>(input, filter, bias, output, stream);   // spatial_strip.cuh:289-301
 //
 // Differences, all documented in the C header:
 //   * the launchers return int8conv_status (void call sites still compile);

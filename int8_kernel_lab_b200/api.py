@@ -4,7 +4,7 @@ Reference interface (header-only templates, compile-time Shape):
     launch_generic<Shape>(input, filter, bias, output, stream = 0)
         include/generic_implicit_gemm.cuh:155-165 (and launch_generic_sm80, :229-238)
     launch_spatial_strip<Shape>(input, filter, bias, output, stream = 0)
-        include/spatial_strip.cuh:528-540
+        include/spatial_strip.cuh:289-301
     kSpatialStripEligible<Shape>
         include/spatial_strip.cuh:11-15
 Here Shape is a runtime ConvShape and the buffers are CUDA tensors (or raw
