@@ -25,6 +25,9 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 DeviceInfo g_devices[kMaxDevices];
+// 1 once g_devices[i] is filled in; the release store publishes the fields
+// to threads that read the flag with acquire (static storage: starts at 0).
+std::atomic<int> g_device_ready[kMaxDevices];
 std::mutex g_device_mutex;
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
@@ -125,9 +128,9 @@ DeviceInfo &device_info() {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices) dev = 0;
   DeviceInfo &d = g_devices[dev];
-  if (d.device != dev) {
+  if (g_device_ready[dev].load(std::memory_order_acquire) == 0) {
     std::lock_guard<std::mutex> lock(g_device_mutex);
-    if (d.device != dev) {
+    if (g_device_ready[dev].load(std::memory_order_relaxed) == 0) {
       cudaDeviceProp prop;
       if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess) {
         d.sm_count = prop.multiProcessorCount;
@@ -137,8 +140,8 @@ DeviceInfo &device_info() {
       void *addr = nullptr;
       if (cudaGetSymbolAddress(&addr, g_device_status) == cudaSuccess)
         d.status = static_cast<uint32_t *>(addr);
-      std::atomic_thread_fence(std::memory_order_release);
       d.device = dev;
+      g_device_ready[dev].store(1, std::memory_order_release);
     }
   }
   return d;

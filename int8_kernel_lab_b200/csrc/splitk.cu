@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <mutex>
 
 #include "conv_common.h"
 #include "int8conv_rules.h"
@@ -413,9 +414,13 @@ static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &
 static const int32_t *cluster_table() {
   static int32_t table[64][9];
   static std::atomic<int> ready[64];
+  static std::mutex fill;
   DeviceInfo &dev = device_info();
   const int d = dev.device & 63;
   if (ready[d].load(std::memory_order_acquire)) return table[d];
+  // One thread fills a device's row; the others wait here and then read it.
+  std::lock_guard<std::mutex> lock(fill);
+  if (ready[d].load(std::memory_order_relaxed)) return table[d];
   const int32_t b200[9] = I8C_B200_CLUSTERS;
   int32_t t[9];
   auto kernel = splitk_kernel<128, false>;
