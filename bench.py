@@ -99,40 +99,100 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled during the timed region.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    The sampler starts before the warm-up and `wait_ready` blocks until its
+    first sample, so a short timed region is not missed while nvidia-smi
+    starts.  Every sample carries nvidia-smi's timestamp; `mark_start` /
+    `mark_stop` bracket the timed region on the host clock, and `stop` keeps
+    the samples inside it, or, for a region shorter than the sampling period,
+    the nearest sample on each side of it."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 20
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_id: str):
         self.proc = None
-        self.out = None
+        self.path = None
+        self.t0 = self.t1 = None
         if shutil.which("nvidia-smi"):
-            self.out = tempfile.TemporaryFile(mode="w+")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-i", gpu_id, "-lms", "20"], stdout=self.out, stderr=subprocess.DEVNULL)
+            fd, self.path = tempfile.mkstemp(prefix="bench_clocks_", suffix=".csv")
+            with os.fdopen(fd, "w") as sink:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                     "-i", gpu_id, "-lms", str(self.PERIOD_MS)],
+                    stdout=sink, stderr=subprocess.DEVNULL)
+
+    def _rows(self):
+        """(host seconds, row) of every complete sample written so far."""
+        with open(self.path) as f:
+            text = f.read()
+        out = []
+        for r in csv.reader(io.StringIO(text)):
+            if len(r) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                continue
+            out.append((ts, [c.strip() for c in r]))
+        return out
+
+    def _wait_for(self, pred, timeout_s: float):
+        deadline = time.time() + timeout_s
+        while time.time() < deadline:
+            if self.proc.poll() is not None or pred(self._rows()):
+                return
+            time.sleep(0.005)
+
+    def wait_ready(self, timeout_s: float = 5.0):
+        if self.proc is not None:
+            self._wait_for(lambda rows: len(rows) > 0, timeout_s)
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_stop(self):
+        self.t1 = time.time()
 
     def stop(self):
         if self.proc is None:
             return None
-        self.proc.terminate()
         try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.out.seek(0)
-        rows = [r for r in csv.reader(io.StringIO(self.out.read())) if len(r) >= 9]
+            if self.t1 is not None:
+                # One sample at or after the end of the region closes the bracket.
+                self._wait_for(lambda rows: any(ts >= self.t1 for ts, _ in rows),
+                               10 * self.PERIOD_MS / 1e3)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.proc.wait()
+            rows = self._rows()
+        finally:
+            os.unlink(self.path)
         if not rows:
             return None
-        sm = sorted(float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]
-                          and "Not" not in r[5 + i]})
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None,
-                "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip() else None,
-                "reasons": reasons, "samples": len(rows)}
+        t0 = self.t0 if self.t0 is not None else rows[0][0]
+        t1 = self.t1 if self.t1 is not None else rows[-1][0]
+        inside = [r for ts, r in rows if t0 <= ts <= t1]
+        chosen = inside
+        if not chosen:
+            # Region shorter than the period: the nearest sample on each side.
+            before = [r for ts, r in rows if ts < t0]
+            after = [r for ts, r in rows if ts > t1]
+            chosen = before[-1:] + after[:1]
+        sm = sorted(float(r[2]) for r in chosen if r[2].replace(".", "").isdigit())
+        reasons = sorted({self.REASONS[i] for r in chosen for i in range(4)
+                          if "Active" in r[6 + i] and "Not" not in r[6 + i]})
+        max_mhz = next((float(r[3]) for r in chosen if r[3].replace(".", "").isdigit()), None)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max_mhz,
+                "reasons": reasons, "samples": len(chosen), "samples_inside": len(inside),
+                "region_ms": round((t1 - t0) * 1e3, 3), "period_ms": self.PERIOD_MS}
 
 
 def shard(n: int, rank: int, world: int):
@@ -286,19 +346,25 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    gpu_uuid = "GPU-" + str(props.uuid) if hasattr(props, "uuid") else str(local)
+    sampler = ClockSampler(gpu_uuid) if rank == 0 else None
+    if sampler:
+        sampler.wait_ready()
     for i in range(args.warmup):
         step(i)
     barrier()
-    gpu_uuid = "GPU-" + str(props.uuid) if hasattr(props, "uuid") else str(local)
-    sampler = ClockSampler(gpu_uuid) if rank == 0 else None
     launches0 = m.launch_count()
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark_start()
     start.record(stream)
     for i in range(args.steps):
         step(i)
     stop.record(stream)
     torch.cuda.synchronize()
+    if sampler:
+        sampler.mark_stop()
     launches = m.launch_count() - launches0
     clocks = sampler.stop() if sampler else None
     elapsed_ms = start.elapsed_time(stop)

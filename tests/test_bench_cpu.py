@@ -1,0 +1,73 @@
+"""bench.py's clock sampler, against a fake nvidia-smi (no GPU needed).
+
+The fake prints one sample every 20 ms in nvidia-smi's CSV form (timestamp
+first, then the fields of ClockSampler.QUERY), so the tests check which
+samples the sampler attributes to a timed region: those inside it, or for a
+region shorter than the period, the nearest one on each side.
+"""
+import os
+import stat
+import sys
+import time
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+
+import bench  # noqa: E402
+
+FAKE = r"""#!/bin/bash
+# Fake nvidia-smi: ignores its arguments, one sample every 20 ms.
+while true; do
+  echo "$(date +'%Y/%m/%d %H:%M:%S.%3N'), 0, 1500, 1965, 900.00, 0x4, Not Active, Not Active, Not Active, Active"
+  sleep 0.02
+done
+"""
+
+
+@pytest.fixture
+def fake_smi(tmp_path, monkeypatch):
+    exe = tmp_path / "nvidia-smi"
+    exe.write_text(FAKE)
+    exe.chmod(exe.stat().st_mode | stat.S_IXUSR)
+    monkeypatch.setenv("PATH", f"{tmp_path}{os.pathsep}{os.environ['PATH']}")
+    return exe
+
+
+def test_samples_inside_a_region(fake_smi):
+    s = bench.ClockSampler("0")
+    s.wait_ready()
+    time.sleep(0.05)
+    s.mark_start()
+    time.sleep(0.2)
+    s.mark_stop()
+    clocks = s.stop()
+    assert clocks["sm_mhz"] == 1500.0 and clocks["sm_max_mhz"] == 1965.0
+    assert clocks["reasons"] == ["sw_power_cap"]
+    assert clocks["samples_inside"] >= 3  # about 10 at a 20 ms period
+    assert clocks["samples"] == clocks["samples_inside"]
+    assert 195 <= clocks["region_ms"] < 1000
+    assert not os.path.exists(s.path)
+
+
+def test_region_shorter_than_the_period_takes_its_neighbours(fake_smi):
+    s = bench.ClockSampler("0")
+    s.wait_ready()
+    time.sleep(0.05)
+    s.mark_start()
+    s.mark_stop()  # a region of microseconds: no sample can fall inside
+    clocks = s.stop()
+    assert clocks["samples_inside"] == 0
+    assert clocks["samples"] == 2  # the last before and the first after
+    assert clocks["sm_mhz"] == 1500.0
+
+
+def test_no_nvidia_smi_gives_no_clocks(tmp_path, monkeypatch):
+    monkeypatch.setenv("PATH", str(tmp_path))
+    s = bench.ClockSampler("0")
+    s.wait_ready()
+    s.mark_start()
+    s.mark_stop()
+    assert s.stop() is None
