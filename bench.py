@@ -251,8 +251,8 @@ def run_reference(args):
     sec = sum(step_s) / len(step_s)
     ops = 2.0 * rows * shape.k * shape.gemm_k
     value = ops / sec / 1e12
-    sample = (f"output rows [0, {rows}) of {args.workload} ({rows / rows_per_image:.3f} of one "
-              f"image, all {shape.k} channels) per step, {threads} threads")
+    sample = (f"output rows [0, {rows}) of {args.workload} ({rows / rows_per_image:.3f} "
+              f"images of {shape.n}, all {shape.k} channels) per step, {threads} threads")
     line = {
         "metric": METRIC, "impl": "reference", "value": value, "unit": "TOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
