@@ -144,6 +144,64 @@ I8C_RULE int64_t i8c_split_tiles(const int8conv_shape *s) {
   return (m + 127) / 128 * ((s->k + 127) / 128);
 }
 
+/* GENERIC's N-tile width: K itself up to 256 (rounded up to `align`), else
+ * the narrowest multiple of `align` that cuts K into ceil(K/256) equal tiles. */
+I8C_RULE int32_t i8c_pick_bn(int32_t k, int32_t align) {
+  if (k <= 256) return (k + align - 1) / align * align;
+  const int32_t tiles = (k + 255) / 256;
+  const int32_t per = (k + tiles - 1) / tiles;
+  return (per + align - 1) / align * align;
+}
+
+/* Tail balancing of the persistent GENERIC/STRIP/HALO grid: with `slots`
+ * tiles running at once, the last wave is partial when num_tiles % slots !=
+ * 0.  Cutting each tile of that wave into f column parts (N = bn/f, 32-column
+ * aligned for the stores) spreads it over more slots.  A part still loads its
+ * tile's whole activation block and filter box, so it costs about 1/f + 0.2
+ * of a tile (B200 sweep of all 51 workloads: parts in several waves, e.g. 98
+ * tiles on 148 CTAs as 392 quarters, were slower).  Spans are in 1/20 tile.
+ * Returns the f in {1, 2, 4} with the shortest span; bn = 0 skips the rule
+ * that bn be a multiple of 32 f. */
+I8C_RULE int32_t i8c_pick_split(int64_t num_tiles, int32_t slots, int32_t bn) {
+  if (slots <= 0) return 1;
+  const int64_t waves = num_tiles / slots;
+  const int64_t rem = num_tiles - waves * slots;
+  int32_t best_f = 1;
+  int64_t best_span = 20 * waves + (rem > 0 ? 20 : 0);
+  for (int32_t f = 2; f <= 4 && rem > 0; f *= 2) {
+    if (bn != 0 && bn % (32 * f) != 0) continue;
+    const int64_t span = 20 * waves + ((f * rem + slots - 1) / slots) * (20 / f + 4);
+    if (span < best_span) {
+      best_span = span;
+      best_f = f;
+    }
+  }
+  return best_f;
+}
+
+/* GENERIC's N-tile width for single CTAs with `slots` of them resident.  A
+ * layer whose 128-row tiles fill less than one wave, and whose width is not
+ * a multiple of 64 (so tail balancing cannot cut it into column parts), runs
+ * narrower N tiles instead, as many as the span model asks for.  A narrow
+ * tile loads only its own filter rows, while each column part of a wide tile
+ * would load the whole filter box (B200, K = 100 on 25 row tiles: four
+ * 32-column tiles 13.4-14.1 us per launch against 16.2 us for one 112-column
+ * tile and 16.2 us for four parts of a 128-column tile). */
+I8C_RULE int32_t i8c_generic_bn(const int8conv_shape *s, int32_t align, int32_t slots) {
+  int32_t bn = i8c_pick_bn(s->k, align);
+  const int64_t m_tiles = ((int64_t)s->n * i8c_out_h(s) * i8c_out_w(s) + 127) / 128;
+  const int64_t tiles = m_tiles * ((s->k + bn - 1) / bn);
+  if (slots > 0 && tiles < slots && i8c_pick_split(tiles, slots, bn) == 1) {
+    const int32_t f = i8c_pick_split(tiles, slots, 0);
+    if (f > 1) {
+      int32_t narrow = ((bn + f - 1) / f + 31) / 32 * 32;
+      if (narrow < 32) narrow = 32;
+      if (narrow < bn) bn = narrow;
+    }
+  }
+  return bn;
+}
+
 /* HALO: positions run over the zero-padded image (Hp x Wp, Hp = out_h +
  * (R-1)*dh, Wp = out_w + (S-1)*dw); one staged halo tile of
  * 128 + (R-1)*dh*Wp + (S-1)*dw pixels per channel block feeds all R*S taps.

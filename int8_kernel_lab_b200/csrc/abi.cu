@@ -160,14 +160,20 @@ int int8conv_select(const int8conv_shape *shape) {
   //    the GPU but a reduction deep enough to split (7x7 and 14x14 layers).
   //    The split must fit in one wave of resident clusters (B200 table):
   //    two waves lost to GENERIC in the sweep (batch8_3x3, darknet_down_52).
+  //  * Except where GENERIC runs narrow N tiles (i8c_generic_bn): those fill
+  //    the GPU without a reduction (4c, K = 100: 13.4-13.8 us per launch
+  //    against 15.1-15.2 us for SPLITK, three interleaved runs on one box).
   if (!i8c_shape_valid(shape)) return INT8CONV_GENERIC;
+  const int32_t clusters[9] = I8C_B200_CLUSTERS;
+  if (i8c_generic_bn(shape, 16, clusters[1]) < i8c_pick_bn(shape->k, 16) &&
+      int8conv_eligible(shape, INT8CONV_GENERIC))
+    return INT8CONV_GENERIC;
   const int64_t m = static_cast<int64_t>(shape->n) * i8c_out_h(shape) * i8c_out_w(shape);
   const int64_t n_tiles = (shape->k + 255) / 256;
   const int64_t tiles = (m + 127) / 128 * n_tiles;
   const int32_t cblk = i8c_channel_block(shape->c);
   const int64_t kblocks =
       static_cast<int64_t>(shape->r) * shape->s * ((shape->c + cblk - 1) / cblk);
-  const int32_t clusters[9] = I8C_B200_CLUSTERS;
   if (int8conv_eligible(shape, INT8CONV_SPLITK) && tiles < 74 && kblocks >= 8 &&
       i8c_split_count(i8c_split_tiles(shape), kblocks, clusters) >= 2)
     return INT8CONV_SPLITK;

@@ -809,13 +809,6 @@ static int pick_cblk(int c) { return i8c_channel_block(c); }
 
 // `align` = 16, or 32 when every 32-column block must hold whole
 // 32-channel vectors (NCHW_VECT_C output).
-static int pick_bn(int k, int align) {
-  if (k <= 256) return (k + align - 1) / align * align;
-  // Balance the N tiles: the smallest multiple of `align` giving ceil(k/256) tiles.
-  const int tiles = (k + 255) / 256;
-  const int per = (k + tiles - 1) / tiles;
-  return (per + align - 1) / align * align;
-}
 
 // Output of a launch: the int32 contract or one of the int8 layouts.
 constexpr int kOutInt32 = 0;
@@ -851,7 +844,10 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   g.dil_w = s.dilation_w;
   g.cblocks = (s.c + cblk - 1) / cblk;
   g.kblocks = s.r * s.s * g.cblocks;
-  g.bn = pick_bn(s.k, out_kind == kOutInt8VectC ? 32 : 16);
+  // Single CTAs of GENERIC may run narrower N tiles (i8c_generic_bn).
+  const int bn_align = out_kind == kOutInt8VectC ? 32 : 16;
+  g.bn = mode == kModeGeneric && !pair ? i8c_generic_bn(&s, bn_align, slots)
+                                       : i8c_pick_bn(s.k, bn_align);
   g.pair = pair ? 1 : 0;
   g.acc_stride = (g.bn + 31) / 32 * 32;
   g.tmem_cols = next_pow2(2 * g.acc_stride);
@@ -902,34 +898,17 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   g.m_tiles = static_cast<int32_t>((positions + tile_rows - 1) / tile_rows);
   g.n_tiles = (s.k + g.bn - 1) / g.bn;
   g.num_tiles = g.m_tiles * g.n_tiles;
-  // Tail balancing: the persistent grid runs `slots` tiles at once, so the
-  // last wave is partial when num_tiles % slots != 0.  Cutting each tile of
-  // that wave into f column parts (N = bn/f, still 32-column aligned for the
-  // stores) spreads it over more slots.  A part still loads its tile's whole
-  // activation block and filter box, so it costs about 1/f + 0.2 of a tile
-  // (B200 sweep of all 51 workloads: parts in several waves, e.g. 98 tiles
-  // on 148 CTAs as 392 quarters, were slower).  Spans are in 1/20 tile.
+  // Tail balancing (i8c_pick_split): the last partial wave's tiles become f
+  // column parts each.
   g.split_from = g.num_tiles;
   g.split_f = 1;
   g.num_units = g.num_tiles;
-  if (slots > 0) {
-    const int waves = g.num_tiles / slots;
-    const int rem = g.num_tiles - waves * slots;
-    int best_f = 1;
-    int best_span = 20 * waves + (rem > 0 ? 20 : 0);
-    for (int f = 2; f <= 4 && rem > 0; f *= 2) {
-      if (g.bn % (32 * f) != 0) continue;
-      const int span = 20 * waves + ((f * rem + slots - 1) / slots) * (20 / f + 4);
-      if (span < best_span) {
-        best_span = span;
-        best_f = f;
-      }
-    }
-    if (best_f > 1) {
-      g.split_f = best_f;
-      g.split_from = g.num_tiles - rem;
-      g.num_units = g.split_from + best_f * rem;
-    }
+  const int best_f = i8c_pick_split(g.num_tiles, slots, g.bn);
+  if (best_f > 1) {
+    const int rem = g.num_tiles % slots;
+    g.split_f = best_f;
+    g.split_from = g.num_tiles - rem;
+    g.num_units = g.split_from + best_f * rem;
   }
   // TMA output stores: GENERIC rows are contiguous in NHWK; the row pitch
   // 4*K must be a multiple of 16 bytes; a 32-column block must not reach into

@@ -71,12 +71,25 @@ def test_splitk_needs_two_kblocks():
 
 
 def test_dispatch_policy_on_baseline():
-    want = {"cfg4b_small_3x3": "splitk", "cfg4c_tail_k100": "splitk",
+    want = {"cfg4b_small_3x3": "splitk", "cfg4c_tail_k100": "generic",
             "cfg5a_stress_3x3": "generic", "cfg5b_dilated_3x3": "generic",
             "cfg3b_pointwise": "generic"}
     table = m.load_workloads()
     for name, fam in want.items():
         assert table[name].select() == fam, name
+
+
+def test_narrow_generic_tiles_take_the_small_odd_k_layer():
+    # GENERIC runs narrow N tiles where its tiles fill less than one wave
+    # and bn is not a multiple of 64 (int8conv_rules.h, i8c_generic_bn); of
+    # the 51 workloads only 4c (K = 100, bn 112 -> four 32-column tiles)
+    # qualifies, and there GENERIC beat SPLITK on B200 (13.4-13.8 against
+    # 15.1-15.2 us per launch).
+    table = m.load_workloads()
+    picked = {name for name, s in table.items()
+              if s.select() == "generic" and s.eligible("splitk") and s.k % 64 != 0
+              and (s.n * s.out_h * s.out_w + 127) // 128 < 148}
+    assert picked == {"cfg4c_tail_k100"}
 
 
 def test_dispatch_needs_a_single_wave_split():
