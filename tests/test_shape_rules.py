@@ -123,3 +123,47 @@ def test_channel_block_choices(tmp_path):
                subprocess.run([str(exe)], capture_output=True, text=True).stdout.split("\n") if line)
     assert got == {16: 32, 32: 32, 48: 64, 64: 64, 80: 128, 96: 128, 128: 128, 160: 128,
                    192: 128, 256: 128, 320: 128, 512: 128}
+
+
+def test_tail_split_and_narrow_tile_rules(tmp_path):
+    # int8conv_rules.h: i8c_pick_split (span model of the column parts) and
+    # i8c_generic_bn (narrow N tiles for sub-wave layers whose BN tail
+    # balancing cannot cut), compiled as C99 and evaluated on known cases.
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no gcc")
+    src = tmp_path / "rules.c"
+    src.write_text(
+        '#include <stdio.h>\n#include "int8conv_rules.h"\n'
+        'int main(void){\n'
+        # (tiles, slots, bn) -> f
+        ' printf("%d %d %d %d %d %d\\n", i8c_pick_split(25, 148, 128), i8c_pick_split(25, 148, 112),'
+        ' i8c_pick_split(25, 148, 0), i8c_pick_split(296, 148, 256), i8c_pick_split(392, 74, 256),'
+        ' i8c_pick_split(120, 148, 256));\n'
+        # BN of GENERIC single CTAs on 148 SMs
+        ' int8conv_shape c4 = {16, 14, 14, 48, 100, 3, 3, 1, 1, 1, 1, 1, 1};\n'
+        ' int8conv_shape c2 = {32, 28, 28, 128, 128, 3, 3, 1, 1, 1, 1, 1, 1};\n'
+        ' int8conv_shape s3 = {8, 14, 14, 128, 128, 3, 3, 1, 1, 1, 1, 1, 1};\n'
+        ' int8conv_shape k300 = {1, 8, 8, 64, 300, 3, 3, 1, 1, 1, 1, 1, 1};\n'
+        ' printf("%d %d %d %d %d\\n", i8c_generic_bn(&c4, 16, 148), i8c_generic_bn(&c2, 16, 148),'
+        ' i8c_generic_bn(&s3, 16, 148), i8c_generic_bn(&c4, 16, 0), i8c_generic_bn(&k300, 16, 148));\n'
+        ' printf("%d %d %d\\n", i8c_pick_bn(100, 16), i8c_pick_bn(100, 32), i8c_pick_bn(700, 16));\n'
+        ' return 0;}\n')
+    exe = tmp_path / "rules"
+    subprocess.run([gcc, "-std=c99", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)],
+                   check=True)
+    lines = subprocess.run([str(exe)], capture_output=True, text=True,
+                           check=True).stdout.split("\n")
+    # 25 tiles on 148 slots: quarters if BN allows (128), none for BN 112, the
+    # model's own choice is quarters; full waves never split; 392 on 74 slots
+    # leaves 22 in the last wave -> halves (span 5.7 tiles; quarters would
+    # need two rounds of parts, 5.9); 120 tiles on 148 stay whole.
+    assert list(map(int, lines[0].split())) == [4, 1, 4, 1, 2, 1]
+    # 4c: 112 -> four 32-column tiles; cfg2 (196 tiles) and the 7-tile 14x14
+    # layer (BN 128 splits into parts) keep their BN; no slots -> no change;
+    # K = 300 on one row tile: BN 160 (two tiles) -> quarters of 40 -> 64.
+    assert list(map(int, lines[1].split())) == [32, 128, 128, 112, 64]
+    # K = 700: three equal tiles of ceil(700 / 3) = 234 -> 240 columns.
+    assert list(map(int, lines[2].split())) == [112, 128, 240]
