@@ -17,6 +17,13 @@ empty and the contract reads "cudnn_not_built"; dispatch_ms maps the winner of
 all four families to its time (the reference's mapping, sweep.py:48, knows
 only strip and generic).
 
+--repeat N runs the case list N times, interleaved (every case once, then
+again), and writes the per-family means: launch-time medians drift by a few
+tenths of a microsecond between runs on one box, and interleaving spreads
+that drift over all cases alike.  A family counts as correct only if every
+repetition validated; the winner, tops and roofline_frac follow the means,
+and a `repeats` column is appended.
+
     python -m int8_kernel_lab_b200.sweep --cases cfg2_mid_3x3,big_3x3_s1 \\
         --output build/dispatch_measurements.csv
 """
@@ -36,6 +43,47 @@ def dispatch_ms(row: dict) -> str:
     return row[column] if column else ""
 
 
+FAMILIES = ("generic", "strip", "halo", "splitk")
+
+
+def _ms(value: str) -> float:
+    try:
+        return float(value)
+    except (TypeError, ValueError):
+        return -1.0
+
+
+def merge_repeats(rows: list) -> dict:
+    """One row from several conv_lab rows of the same case: mean launch times
+    (-1 unless every repetition timed the family), correctness only if every
+    repetition validated, winner / tops / roofline_frac from the means."""
+    merged = dict(rows[0])
+    for column in [f + "_ms" for f in FAMILIES] + ["graph_ms"]:
+        if column not in merged:
+            continue
+        values = [_ms(r.get(column)) for r in rows]
+        merged[column] = ("%.6g" % (sum(values) / len(values))
+                          if all(v >= 0 for v in values) else "-1")
+    for f in FAMILIES:
+        column = f + "_correct"
+        if column in merged:
+            merged[column] = "1" if all(r.get(column) == "1" for r in rows) else "0"
+    timed = {f: _ms(merged[f + "_ms"]) for f in FAMILIES if f + "_ms" in merged}
+    timed = {f: v for f, v in timed.items() if v >= 0}
+    if "winner" in merged:
+        old_winner = rows[0].get("winner")
+        merged["winner"] = min(timed, key=timed.get) if timed else "none"
+        first_ms = _ms(rows[0].get(old_winner + "_ms", "")) if old_winner in FAMILIES else -1.0
+        if timed and first_ms > 0:
+            # tops and roofline_frac scale with the winner's time.
+            scale = first_ms / timed[merged["winner"]]
+            for column in ("tops", "roofline_frac"):
+                if _ms(merged.get(column)) >= 0:
+                    merged[column] = "%.6g" % (_ms(merged[column]) * scale)
+    merged["repeats"] = str(len(rows))
+    return merged
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--configs", default=str(PKG / "workloads.csv"), type=Path)
@@ -52,7 +100,11 @@ def main(argv=None) -> int:
     ap.add_argument("--arch", default="sm_100a")
     ap.add_argument("--with-cudnn", action="store_true")
     ap.add_argument("--cudnn-root", default="")
+    ap.add_argument("--repeat", type=int, default=1,
+                    help="run the case list this many times, interleaved, and write means")
     args = ap.parse_args(argv)
+    if args.repeat < 1:
+        raise SystemExit("--repeat must be at least 1")
     if args.arch not in ("sm_100a", "sm_100"):
         raise SystemExit(f"--arch {args.arch}: this engine is built for sm_100a only")
     with open(args.configs, newline="") as stream:
@@ -62,39 +114,48 @@ def main(argv=None) -> int:
     if unknown:
         raise SystemExit(f"unknown cases: {', '.join(unknown)}")
     args.output.parent.mkdir(parents=True, exist_ok=True)
-    measurements = []
+    runs = {}  # case -> list of conv_lab rows, one per repetition
     status = 0
     shapes = {r["name"]: r for r in rows}
-    for case in requested:
-        r = shapes[case]
-        oh = int((int(r["h"]) + 2 * int(r["pad_h"]) - int(r["dilation_h"]) * (int(r["r"]) - 1) - 1)
-                 / int(r["stride_h"])) + 1
-        ow = int((int(r["w"]) + 2 * int(r["pad_w"]) - int(r["dilation_w"]) * (int(r["s"]) - 1) - 1)
-                 / int(r["stride_w"])) + 1
-        ops = 2.0 * int(r["n"]) * oh * ow * int(r["k"]) * int(r["c"]) * int(r["r"]) * int(r["s"])
-        extra = ["--validate-samples", "200000"] if ops > args.full_validate_ops else []
-        result = subprocess.run(
-            [args.conv_lab, "--case", case, "--config", str(args.configs), "--strategy",
-             args.strategy, "--iterations", str(args.iterations), "--warmup", str(args.warmup),
-             "--values", args.values, "--pairing", args.pairing, "--csv"] + extra,
-            text=True, capture_output=True)
-        if result.returncode != 0:
-            status = 1
-            sys.stderr.write(result.stderr)
-        lines = result.stdout.strip().splitlines()
-        if len(lines) < 2:
-            print(f"{case}: conv_lab failed (exit {result.returncode})", file=sys.stderr)
-            continue
-        measurement = next(csv.DictReader(lines))
-        if args.with_cudnn:
-            measurement.update(dispatch_ms=dispatch_ms(measurement), cudnn_ms="",
-                               cudnn_over_dispatch="", comparison_contract="cudnn_not_built")
-        measurements.append(measurement)
-        with open(args.output, "w", newline="") as stream:
-            writer = csv.DictWriter(stream, fieldnames=measurements[0].keys())
-            writer.writeheader()
-            writer.writerows(measurements)
-        print(f"{case}: wrote {args.output}", flush=True)
+    for rep in range(args.repeat):
+        for case in requested:
+            r = shapes[case]
+            oh = int((int(r["h"]) + 2 * int(r["pad_h"]) -
+                      int(r["dilation_h"]) * (int(r["r"]) - 1) - 1) / int(r["stride_h"])) + 1
+            ow = int((int(r["w"]) + 2 * int(r["pad_w"]) -
+                      int(r["dilation_w"]) * (int(r["s"]) - 1) - 1) / int(r["stride_w"])) + 1
+            ops = (2.0 * int(r["n"]) * oh * ow * int(r["k"]) * int(r["c"]) * int(r["r"]) *
+                   int(r["s"]))
+            extra = ["--validate-samples", "200000"] if ops > args.full_validate_ops else []
+            result = subprocess.run(
+                [args.conv_lab, "--case", case, "--config", str(args.configs), "--strategy",
+                 args.strategy, "--iterations", str(args.iterations), "--warmup",
+                 str(args.warmup), "--values", args.values, "--pairing", args.pairing,
+                 "--csv"] + extra,
+                text=True, capture_output=True)
+            if result.returncode != 0:
+                status = 1
+                sys.stderr.write(result.stderr)
+            lines = result.stdout.strip().splitlines()
+            if len(lines) < 2:
+                print(f"{case}: conv_lab failed (exit {result.returncode})", file=sys.stderr)
+                continue
+            runs.setdefault(case, []).append(next(csv.DictReader(lines)))
+            measurements = []
+            for name in requested:
+                if name not in runs:
+                    continue
+                m = merge_repeats(runs[name]) if args.repeat > 1 else dict(runs[name][0])
+                if args.with_cudnn:
+                    m.update(dispatch_ms=dispatch_ms(m), cudnn_ms="", cudnn_over_dispatch="",
+                             comparison_contract="cudnn_not_built")
+                measurements.append(m)
+            with open(args.output, "w", newline="") as stream:
+                writer = csv.DictWriter(stream, fieldnames=measurements[0].keys())
+                writer.writeheader()
+                writer.writerows(measurements)
+            suffix = f" (repetition {rep + 1}/{args.repeat})" if args.repeat > 1 else ""
+            print(f"{case}: wrote {args.output}{suffix}", flush=True)
     return status
 
 
