@@ -71,13 +71,22 @@ int8conv_status launch_host_pipeline(int strategy, const int8conv_shape &s, cons
   const size_t in_image = static_cast<size_t>(s.h) * s.w * s.c;
   const size_t out_image = static_cast<size_t>(out_h) * out_w * s.k;
   auto ok = [](cudaError_t e) { return e == cudaSuccess; };
+  // On an error part-way through, copies already queued may still be reading
+  // or writing the caller's host buffers: wait for them before returning, so
+  // the caller may free those buffers as soon as the call fails.
+  auto fail = [&](int8conv_status st) {
+    cudaStreamSynchronize(p.h2d);
+    cudaStreamSynchronize(p.compute);
+    cudaStreamSynchronize(p.d2h);
+    return st;
+  };
   // Everything the caller queued on `stream` before this call happens first.
   if (!ok(cudaEventRecord(p.start, stream)) || !ok(cudaStreamWaitEvent(p.h2d, p.start, 0)))
     return INT8CONV_CUDA_ERROR;
   const size_t filter_bytes = static_cast<size_t>(s.k) * s.r * s.s * s.c;
   if (!ok(cudaMemcpyAsync(dw, hw, filter_bytes, cudaMemcpyHostToDevice, p.h2d)) ||
       !ok(cudaMemcpyAsync(db, hb, sizeof(int32_t) * s.k, cudaMemcpyHostToDevice, p.h2d)))
-    return INT8CONV_CUDA_ERROR;
+    return fail(INT8CONV_CUDA_ERROR);
   int first = 0;
   for (int c = 0; c < chunks; ++c) {
     const int last = static_cast<int>((static_cast<int64_t>(s.n) * (c + 1)) / chunks);
@@ -89,20 +98,20 @@ int8conv_status launch_host_pipeline(int strategy, const int8conv_shape &s, cons
     if (!ok(cudaMemcpyAsync(dx + x_off, hx + x_off, images * in_image, cudaMemcpyHostToDevice,
                             p.h2d)) ||
         !ok(cudaEventRecord(p.in[c], p.h2d)) || !ok(cudaStreamWaitEvent(p.compute, p.in[c], 0)))
-      return INT8CONV_CUDA_ERROR;
+      return fail(INT8CONV_CUDA_ERROR);
     const int fam = strategy == INT8CONV_AUTO ? int8conv_select(&part) : strategy;
     const int8conv_status st = int8conv_launch(fam, &part, dx + x_off, dw, db, dy + y_off, nullptr,
                                                0, p.compute);
-    if (st != INT8CONV_OK) return st;
+    if (st != INT8CONV_OK) return fail(st);
     if (!ok(cudaEventRecord(p.done[c], p.compute)) ||
         !ok(cudaStreamWaitEvent(p.d2h, p.done[c], 0)) ||
         !ok(cudaMemcpyAsync(hy + y_off, dy + y_off, images * out_image * sizeof(int32_t),
                             cudaMemcpyDeviceToHost, p.d2h)))
-      return INT8CONV_CUDA_ERROR;
+      return fail(INT8CONV_CUDA_ERROR);
     first = last;
   }
   if (!ok(cudaEventRecord(p.out, p.d2h)) || !ok(cudaStreamWaitEvent(stream, p.out, 0)))
-    return INT8CONV_CUDA_ERROR;
+    return fail(INT8CONV_CUDA_ERROR);
   return INT8CONV_OK;
 }
 
