@@ -188,7 +188,9 @@ int8conv_status int8conv_launch_requant(int strategy, const int8conv_shape *shap
  * after enqueueing: `stream` waits for every copy and launch, so synchronising
  * it (or any later work on it) sees the finished host output.  The chunk
  * launches run strategy `strategy` (or the dispatch policy for INT8CONV_AUTO)
- * on each group's shape. */
+ * on each group's shape.  On an error after the first copy was queued, the
+ * call first waits for the copies and launches it already queued, so the
+ * host buffers are no longer in use when it returns. */
 int8conv_status int8conv_launch_host(int strategy, const int8conv_shape *shape,
                                      const int8_t *host_input, const int8_t *host_filter,
                                      const int32_t *host_bias, int32_t *host_output,
