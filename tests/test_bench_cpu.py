@@ -71,3 +71,37 @@ def test_no_nvidia_smi_gives_no_clocks(tmp_path, monkeypatch):
     s.mark_start()
     s.mark_stop()
     assert s.stop() is None
+
+
+def _run_bench(args, env_extra=None, timeout=600):
+    import json
+    import subprocess
+    env = dict(os.environ, **(env_extra or {}))
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), *args], capture_output=True,
+                         text=True, timeout=timeout, env=env, cwd=str(ROOT))
+    lines = [l for l in out.stdout.splitlines() if l.strip()]
+    return out.returncode, [json.loads(l) for l in lines], out.stderr
+
+
+def test_reference_arm_prints_one_line():
+    # The reference's own CPU implementation (oracle/_ref when built from the
+    # reference sources, else the oracle port) on a small workload.
+    rc, lines, err = _run_bench(["--impl", "reference", "--workload", "cfg1_smoke",
+                                 "--steps", "2", "--warmup", "1"])
+    assert rc == 0, err
+    assert len(lines) == 1
+    line = lines[0]
+    assert line["impl"] == "reference" and line["unit"] == "TOPS" and line["value"] > 0
+    assert line["higher_is_better"] is True and line["steps"] == 2 and line["warmup"] == 1
+    assert line["config"]["workload"] == "cfg1_smoke"
+    assert line["cpu_baseline"]["kind"] in ("reference", "port")
+    assert line["cpu_baseline"]["value"] == line["value"] and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "TOPS", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    rc, lines, err = _run_bench(["--impl", "reference", "--gpus", "2", "--steps", "1",
+                                 "--warmup", "0"], {"RANK": "1", "WORLD_SIZE": "2"})
+    assert rc == 0, err
+    assert lines == []
