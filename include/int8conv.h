@@ -222,6 +222,14 @@ void int8conv_debug_starve_producer(int on);
  * computes identical results; the choice only moves performance. */
 int8conv_status int8conv_set_cta_pairing(int mode);
 
+/* Activation staging of GENERIC (process-wide): 0 = automatic (the TMA
+ * im2col tensor map wherever it can encode the shape, else the gather warp),
+ * 1 = the gather warp for every shape.  Both compute identical results; the
+ * gather exists for shapes beyond the im2col limits (stride > 8, pad > 127,
+ * (R-1)*dilation > 127), and forcing it lets tests compare the two stagings
+ * on any shape. */
+int8conv_status int8conv_set_generic_staging(int mode);
+
 /* Number of kernels this library has launched in this process. */
 uint64_t int8conv_launch_count(void);
 

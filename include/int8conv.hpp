@@ -81,8 +81,11 @@ template <class Shape>
 inline int8conv_status launch_generic(const int8_t *input, const int8_t *filter,
                                       const int32_t *bias, int32_t *output,
                                       cudaStream_t stream = 0) {
+  // Every shape ConvShape accepts (c % 16 == 0, non-empty output) with its
+  // fields in the engine's ranges; stride, pad and dilation are unbounded
+  // within them, as in the reference's generic launcher.
   static_assert(int8conv_detail::generic_eligible<Shape>(),
-                "shape exceeds the TMA limits of the generic kernel");
+                "shape fields out of the generic kernel's range");
   constexpr int8conv_shape shape = Shape::runtime();
   return int8conv_launch_generic(&shape, input, filter, bias, output, stream);
 }

@@ -20,9 +20,10 @@
 #define I8C_RULE static inline
 #endif
 
-/* TMA / kernel-geometry limits shared by every family.  They bound the
- * im2col bounding-box corners ([-128,127] for a 4-D tensor map), the im2col
- * tap offsets and the traversal strides (1..8) of the activation tensor map. */
+/* TMA limits of the activation im2col tensor map.  They bound the im2col
+ * bounding-box corners ([-128,127] for a 4-D tensor map), the im2col tap
+ * offsets and the traversal strides (1..8).  Shapes beyond them run GENERIC's
+ * gather staging instead (i8c_im2col_ok). */
 #define I8C_MAX_PAD 127
 #define I8C_MAX_TAP_SPAN 127
 #define I8C_MAX_STRIDE 8
@@ -65,10 +66,9 @@ I8C_RULE int32_t i8c_upper_corner(int32_t extent, int32_t pad, int32_t stride,
 
 I8C_RULE int i8c_corner_ok(int32_t v) { return v >= -128 && v <= 127; }
 
-/* GENERIC: every valid shape whose activation tensor map can be encoded.
- * Replaces the reference's generic family (generic_implicit_gemm.cuh), which
- * accepted every shape with c % 16 == 0. */
-I8C_RULE int i8c_generic_eligible(const int8conv_shape *s) {
+/* 1 if the activations of the shape can be staged through a TMA im2col tensor
+ * map (GENERIC's fast staging; required by STRIP, HALO and SPLITK). */
+I8C_RULE int i8c_im2col_ok(const int8conv_shape *s) {
   return i8c_shape_valid(s) && s->pad_h <= I8C_MAX_PAD && s->pad_w <= I8C_MAX_PAD &&
          s->stride_h <= I8C_MAX_STRIDE && s->stride_w <= I8C_MAX_STRIDE &&
          (int64_t)(s->r - 1) * s->dilation_h <= I8C_MAX_TAP_SPAN &&
@@ -77,6 +77,12 @@ I8C_RULE int i8c_generic_eligible(const int8conv_shape *s) {
          i8c_corner_ok(i8c_upper_corner(s->h, s->pad_h, s->stride_h, i8c_out_h(s)));
 }
 
+/* GENERIC: every valid shape, like the reference's generic family
+ * (generic_implicit_gemm.cuh, whose gather at :46-69 handles any stride, pad
+ * and dilation; conv_shape.cuh:34-35 are its only conditions).  Shapes the
+ * im2col map cannot encode are staged by a gather warp instead of TMA. */
+I8C_RULE int i8c_generic_eligible(const int8conv_shape *s) { return i8c_shape_valid(s); }
+
 /* STRIP: one TMA-loaded row strip of (128 + S - 1) padded-row pixels is
  * reused across the S filter columns.  Needs unit horizontal stride and
  * dilation (the reference's own conditions, spatial_strip.cuh:11-15) and
@@ -84,7 +90,7 @@ I8C_RULE int i8c_generic_eligible(const int8conv_shape *s) {
  * here; out_w % 128 and the r == 3 restriction are dropped because the B200
  * kernel tiles the padded row instead of whole 128-pixel output rows. */
 I8C_RULE int i8c_strip_eligible(const int8conv_shape *s) {
-  return i8c_generic_eligible(s) && s->stride_w == 1 && s->dilation_w == 1 &&
+  return i8c_im2col_ok(s) && s->stride_w == 1 && s->dilation_w == 1 &&
          s->s >= 2 && s->s <= 16 &&
          i8c_corner_ok(i8c_upper_corner(s->w, s->pad_w, 1, i8c_out_w(s) + s->s - 1));
 }
@@ -116,9 +122,9 @@ I8C_RULE int32_t i8c_channel_block(int32_t c) {
 
 /* SPLITK: the R*S*C reduction of each output tile is split across the CTAs
  * of a cluster, so there must be at least two k-blocks (tap x channel block)
- * to split.  Same TMA limits as GENERIC. */
+ * to split.  Activations come through the im2col map. */
 I8C_RULE int i8c_splitk_eligible(const int8conv_shape *s) {
-  return i8c_generic_eligible(s) &&
+  return i8c_im2col_ok(s) &&
          (int64_t)s->r * s->s * ((s->c + i8c_channel_block(s->c) - 1) / i8c_channel_block(s->c)) >= 2;
 }
 
@@ -208,7 +214,7 @@ I8C_RULE int32_t i8c_generic_bn(const int8conv_shape *s, int32_t align, int32_t 
  * Needs unit strides and a staged tile of at most 512 pixels (small spatial
  * layers). */
 I8C_RULE int i8c_halo_eligible(const int8conv_shape *s) {
-  return i8c_generic_eligible(s) && s->stride_h == 1 && s->stride_w == 1 &&
+  return i8c_im2col_ok(s) && s->stride_h == 1 && s->stride_w == 1 &&
          128 + (int64_t)(s->r - 1) * s->dilation_h *
                    (i8c_out_w(s) + (int64_t)(s->s - 1) * s->dilation_w) +
                  (int64_t)(s->s - 1) * s->dilation_w <= 512 &&

@@ -10,7 +10,8 @@ from ._abi import (AUTO, GENERIC, HALO, SPLITK, STRIP, STRATEGIES, Int8ConvError
 from .api import (conv2d, debug_starve_producer, device_status, launch,  # noqa: F401
                   launch_count, launch_host, launch_generic, launch_generic_sm80, launch_requant,
                   launch_spatial_strip,
-                  set_cta_pairing, set_wait_limit_ns, spatial_strip_eligible, workspace_bytes)
+                  set_cta_pairing, set_generic_staging, set_wait_limit_ns,
+                  spatial_strip_eligible, workspace_bytes)
 from .data import REFERENCE_SEED, make_inputs  # noqa: F401
 from .shape import (BASELINE_CASES, ConvShape, baseline_shapes, load_workloads)  # noqa: F401
 

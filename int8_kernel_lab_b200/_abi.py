@@ -87,6 +87,7 @@ SIGNATURES = {
     "int8conv_debug_starve_producer": (None, [ctypes.c_int]),
     "int8conv_launch_count": (ctypes.c_uint64, []),
     "int8conv_set_cta_pairing": (ctypes.c_int, [ctypes.c_int]),
+    "int8conv_set_generic_staging": (ctypes.c_int, [ctypes.c_int]),
 }
 
 

@@ -182,5 +182,15 @@ def set_cta_pairing(mode: str) -> None:
     _abi.check(_abi.lib.int8conv_set_cta_pairing(PAIRING[mode]), "set_cta_pairing")
 
 
+STAGING = {"auto": 0, "gather": 1}
+
+
+def set_generic_staging(mode: str) -> None:
+    """'auto' | 'gather': how GENERIC stages activations ('auto' uses the TMA
+    im2col map wherever it can encode the shape; 'gather' uses the gather warp
+    for every shape)."""
+    _abi.check(_abi.lib.int8conv_set_generic_staging(STAGING[mode]), "set_generic_staging")
+
+
 def debug_starve_producer(on: bool) -> None:
     _abi.lib.int8conv_debug_starve_producer(1 if on else 0)

@@ -14,6 +14,7 @@ extern std::atomic<uint64_t> g_wait_limit_ns;
 extern std::atomic<uint32_t> g_starve;
 extern std::atomic<uint64_t> g_launches;
 extern std::atomic<int> g_pairing;
+extern std::atomic<int> g_staging;
 }  // namespace i8c
 
 namespace {
@@ -26,7 +27,7 @@ bool aligned16(const void *p) { return p != nullptr && (reinterpret_cast<uintptr
 // and encoding descriptors again.  Thread-local, so no locking; a plan only
 // depends on the key's fields (the tensor maps hold the buffer addresses).
 struct PlanKey {
-  int32_t device, strategy, pairing, out_kind;
+  int32_t device, strategy, pairing, staging, out_kind;
   int8conv_shape shape;
   int32_t zero_point, relu;
   const void *x, *w, *b, *y, *multiplier, *exponent;
@@ -46,6 +47,7 @@ PlanKey plan_key(int strategy, const int8conv_shape &s, const void *x, const voi
   k.device = i8c::device_info().device;
   k.strategy = strategy;
   k.pairing = i8c::pairing_mode();
+  k.staging = i8c::staging_mode();
   k.out_kind = out_kind;
   k.shape = s;
   k.x = x;
@@ -165,7 +167,12 @@ int int8conv_select(const int8conv_shape *shape) {
   //    against 15.1-15.2 us for SPLITK, three interleaved runs on one box).
   if (!i8c_shape_valid(shape)) return INT8CONV_GENERIC;
   const int32_t clusters[9] = I8C_B200_CLUSTERS;
-  if (i8c_generic_bn(shape, 16, clusters[1]) < i8c_pick_bn(shape->k, 16) &&
+  // GENERIC's narrow-tile rule runs with the current device's SM count (the
+  // kernel's planner uses it); the B200 count where no sm_100 device is
+  // current (host-only use).  The split-K table below is B200's.
+  int slots = clusters[1];
+  if (i8c::check_device() == INT8CONV_OK) slots = i8c::device_info().sm_count;
+  if (i8c_generic_bn(shape, 16, slots) < i8c_pick_bn(shape->k, 16) &&
       int8conv_eligible(shape, INT8CONV_GENERIC))
     return INT8CONV_GENERIC;
   const int64_t m = static_cast<int64_t>(shape->n) * i8c_out_h(shape) * i8c_out_w(shape);
@@ -345,6 +352,12 @@ uint64_t int8conv_launch_count(void) { return i8c::g_launches.load(); }
 int8conv_status int8conv_set_cta_pairing(int mode) {
   if (mode < 0 || mode > 2) return INT8CONV_BAD_ARGUMENT;
   i8c::g_pairing.store(mode);
+  return INT8CONV_OK;
+}
+
+int8conv_status int8conv_set_generic_staging(int mode) {
+  if (mode < 0 || mode > 1) return INT8CONV_BAD_ARGUMENT;
+  i8c::g_staging.store(mode);
   return INT8CONV_OK;
 }
 

@@ -15,6 +15,7 @@ namespace i8c {
 struct ConvGeom {
   int32_t M;         // n * out_h * out_w
   int32_t K;         // output channels (GEMM N)
+  int32_t H, W, C;   // input height, width, channels (gather staging)
   int32_t P, Q;      // out_h, out_w
   int32_t PQ;        // out_h * out_w
   int32_t R, S;
@@ -45,6 +46,9 @@ struct ConvGeom {
   int32_t strip_px;  // pixels per staged load (128 + largest tap shift)
   int32_t a_rows;    // rows reserved per staged tile (strip_px rounded up to 8)
   int32_t a_stages;  // staged-tile ring depth
+  // GATHER: k-blocks whose copies may still be in flight when the next one
+  // is issued (1..3, fewer than `stages`).
+  int32_t gather_lag;
 };
 
 // Failure-detection controls passed to every kernel.

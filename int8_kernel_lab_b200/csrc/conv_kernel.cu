@@ -53,6 +53,11 @@
 //   (Hp x Wp positions per image); one staged tile of 128 + (R-1)*dh*Wp +
 //   (S-1)*dw positions per channel block feeds all R*S taps, tap (r, s)
 //   reading it r*dh*Wp + s*dw rows further on.
+// GATHER (GENERIC on shapes the im2col tensor map cannot encode: stride > 8,
+//   pad > 127, tap span > 127): warp 0's 32 lanes stage the same 128-row
+//   tiles with asynchronous 16-byte copies into the same swizzled layout
+//   (gather_producer); the filter, the MMA issuer and the epilogue are
+//   GENERIC's.  Single CTAs only.
 // The reference's odd-K epilogue bug (generic_implicit_gemm.cuh:218-225) has
 // no counterpart: every column < K is stored.
 #include <cuda.h>
@@ -90,6 +95,9 @@ constexpr uint32_t kOneCtaPerSm = kMaxSmem / 2 + 1024;
 constexpr int kModeGeneric = 0;  // one im2col tile per tap and channel block
 constexpr int kModeStrip = 1;    // one row strip per (filter row, channel block)
 constexpr int kModeHalo = 2;     // one halo tile per channel block
+constexpr int kModeGather = 3;   // GENERIC's tiles staged by a gather warp (any shape)
+// Row table of the gather warp: one int4 per row of a 128-row tile.
+constexpr uint32_t kGatherRowTable = kBlockM * 16;
 // Largest staged tile (rows of CBLK bytes): im2col loads move at most 1024
 // pixels, and a few stages must fit in shared memory.
 constexpr int kMaxStagedRows = 512;
@@ -98,11 +106,12 @@ constexpr int kMaxStagedRows = 512;
 struct SmemPlan {
   uint32_t a_bytes, b_bytes;  // one stage of A / B (this CTA's share)
   uint32_t a_off, b_off, stage_off, bar_off;
+  uint32_t rows_off;          // gather row table (GATHER only)
   uint32_t total;             // bytes requested at launch (incl. alignment slack)
 };
 
 __host__ __device__ inline SmemPlan smem_plan(int cblk, int b_rows, int a_rows, int a_stages,
-                                              int b_stages) {
+                                              int b_stages, bool gather = false) {
   SmemPlan p;
   p.a_bytes = a_rows * cblk;
   p.b_bytes = b_rows * cblk;
@@ -114,7 +123,8 @@ __host__ __device__ inline SmemPlan smem_plan(int cblk, int b_rows, int a_rows, 
   p.bar_off = p.stage_off + kEpilogueStaging;
   // a_full/a_empty[a_stages], b_full/b_empty[b_stages], tfull[2], tempty[2], drain, slot
   const uint32_t bar_bytes = (2 * a_stages + 2 * b_stages + 5) * 8 + 8;
-  p.total = 1024 + p.bar_off + bar_bytes;
+  p.rows_off = (p.bar_off + bar_bytes + 15) & ~15u;
+  p.total = 1024 + (gather ? p.rows_off + kGatherRowTable : p.bar_off + bar_bytes);
   return p;
 }
 
@@ -167,6 +177,136 @@ __device__ __forceinline__ void commit_to(uint64_t *bar) {
     umma_commit(bar);
 }
 
+// GATHER producer (warp 0, all 32 lanes): GENERIC's A tiles for shapes the
+// im2col tensor map cannot encode (stride > 8, pad > 127, tap span > 127, or a
+// bounding-box corner out of range), in the same swizzled layout TMA would
+// write, so the MMA issuer and the epilogue are GENERIC's.  This is the
+// reference's gather (generic_implicit_gemm.cuh:46-69: 16-byte vectors at
+// (n, iy, ix, c), zero for padding taps and rows past M) done with
+// asynchronous 16-byte copies that keep `g.gather_lag` k-blocks in flight.
+//
+// Per tile the warp tabulates each row's image offset and input origin
+// (img*H, oy*sh - ph, ox*sw - pw) in shared memory; per k-block (tap r,s x
+// channel block) lane (row sub-index, 16-byte chunk) copies its chunk of
+// every (32 / chunks)-th row.  A k-block is published once every lane's
+// copies have landed: each lane fences its generic-proxy writes for the
+// tensor cores' async-proxy reads and arrives on the stage's barrier, which
+// also counts the filter tile's TMA bytes (lane 0 arms and issues it).
+template <int CBLK>
+__device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t *__restrict__ x,
+                                                const CUtensorMap *tmap_w, uint8_t *a_ring,
+                                                uint8_t *b_ring, const SmemPlan &plan,
+                                                int4 *rowtab, uint64_t *b_full,
+                                                uint64_t *b_empty, const RunCtl &ctl,
+                                                const WaitCtx &wctx, int tile_first,
+                                                int tile_step, int lane) {
+  constexpr int kChunks = CBLK / 16;          // 16-byte chunks per row
+  constexpr int kRowsPerPass = 32 / kChunks;  // rows one warp-wide pass covers
+  constexpr int kPasses = kBlockM / kRowsPerPass;
+  constexpr uint32_t kSwMask = kChunks - 1;   // 128/64/32-byte swizzle: chunk ^= row bits
+  const int chunk = lane % kChunks;
+  const int rsub = lane / kChunks;
+  const int lag = g.gather_lag;
+  Ring rb;           // next stage to fill
+  Ring rp;           // oldest stage filled but not yet published
+  int pending = 0;   // k-blocks issued and not yet published
+  long armed_b = 0;  // filter loads issued (lane 0)
+  auto publish = [&]() {
+    // This lane's copies of the k-block are complete (cp_async_wait);
+    // make them visible to the async proxy, then arrive.
+    fence_proxy_async_smem();
+    mbar_arrive(&b_full[rp.stage]);
+    rp.next(g.stages);
+    --pending;
+  };
+  bool ok = true;
+  for (int tile = tile_first; tile < g.num_units && ok; tile += tile_step) {
+    const Unit t = unit_at(g, tile);
+    const int m0 = t.m_tile * kBlockM;
+    // Row table of this tile (every lane has issued the previous tile's
+    // copies, whose source addresses are already in registers).
+    __syncwarp();
+    for (int i = lane; i < kBlockM; i += 32) {
+      const int m = m0 + i;
+      int4 e = make_int4(0, -(1 << 30), -(1 << 30), 0);  // rows past M: every tap is padding
+      if (m < g.M) {
+        const int img = m / g.PQ;
+        const int rem = m - img * g.PQ;
+        const int oy = rem / g.Q;
+        const int ox = rem - oy * g.Q;
+        e = make_int4(img * g.H, oy * g.stride_h - g.pad_h, ox * g.stride_w - g.pad_w, 0);
+      }
+      rowtab[i] = e;
+    }
+    __syncwarp();
+    int cb = 0, r = 0, s = 0, tap = 0;
+    for (int kb = 0; kb < g.kblocks; ++kb) {
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(&b_empty[rb.stage], rb.phase ^ 1u, wctx, kStatusTimeoutEmpty))) {
+        ok = false;
+        break;
+      }
+      if (!ctl.starve) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&b_full[rb.stage], plan.b_bytes);
+          tma_load_3d(b_ring + rb.stage * plan.b_bytes, tmap_w, &b_full[rb.stage], cb * CBLK, tap,
+                      t.n0);
+          ++armed_b;
+        }
+        const uint32_t a_base = smem_u32(a_ring + rb.stage * plan.a_bytes);
+        const int dy = r * g.dil_h;
+        const int dx = s * g.dil_w;
+        const int c_off = cb * CBLK + chunk * 16;
+        const bool c_ok = c_off < g.C;
+#pragma unroll 8
+        for (int i = 0; i < kPasses; ++i) {
+          const int row = rsub + i * kRowsPerPass;
+          const int4 e = rowtab[row];
+          const int iy = e.y + dy;
+          const int ix = e.z + dx;
+          const bool in = c_ok && static_cast<unsigned>(iy) < static_cast<unsigned>(g.H) &&
+                          static_cast<unsigned>(ix) < static_cast<unsigned>(g.W);
+          const int8_t *src =
+              in ? x + (static_cast<int64_t>(e.x + iy) * g.W + ix) * g.C + c_off : x;
+          const uint32_t off = static_cast<uint32_t>(row * CBLK + chunk * 16);
+          cp_async_16(a_base + (off ^ (((off >> 7) & kSwMask) << 4)), src, in ? 16u : 0u);
+        }
+        cp_async_commit();
+        ++pending;
+        if (pending > lag) {
+          if (lag >= 3)
+            cp_async_wait<3>();
+          else if (lag == 2)
+            cp_async_wait<2>();
+          else
+            cp_async_wait<1>();
+          publish();
+        }
+      }
+      rb.next(g.stages);
+      if (++cb == g.cblocks) {
+        cb = 0;
+        ++tap;
+        if (++s == g.S) {
+          s = 0;
+          ++r;
+        }
+      }
+    }
+  }
+  // Publish what is still in flight (also on the error path: the shared
+  // memory must not be released under a pending copy).
+  cp_async_wait<0>();
+  while (pending > 0) publish();
+  // The filter loads armed most recently land before the CTA exits.
+  if (lane == 0) {
+    for (long i = 0, n = armed_b < g.stages ? armed_b : g.stages; i < n; ++i) {
+      rb.prev(g.stages);
+      mbar_wait(&b_full[rb.stage], rb.phase, wctx, kStatusTimeoutTeardown);
+    }
+  }
+}
+
 // Requantisation of one thread's 32 accumulators (this warp's row, a
 // 32-column block): four channels per word.  `table` holds the block's 32
 // channel entries (rq_entry, bias included); every lane reads each entry with
@@ -216,8 +356,8 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
     conv_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_w,
                 const __grid_constant__ CUtensorMap tmap_y, const ConvGeom g,
-                const int32_t *__restrict__ bias, int32_t *__restrict__ out, const RunCtl ctl,
-                const Requant rq) {
+                const int8_t *__restrict__ x, const int32_t *__restrict__ bias,
+                int32_t *__restrict__ out, const RunCtl ctl, const Requant rq) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment: the SW128 atom (8 rows x 128 B) starts on it.  The
   // offset is the same in both CTAs of a pair (same kernel, same smem size).
@@ -227,10 +367,12 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
   constexpr bool STRIP = MODE == kModeStrip;
   constexpr bool HALO = MODE == kModeHalo;
   constexpr bool SHIFT = STRIP || HALO;  // A operand = shifted views of one staged tile
+  constexpr bool GATHER = MODE == kModeGather;
+  static_assert(!(GATHER && PAIR), "the gather staging runs single CTAs");
   const int a_stages = SHIFT ? g.a_stages : g.stages;
   const int a_rows = SHIFT ? g.a_rows : kBlockM;
   const int b_rows = PAIR ? g.bn / 2 : g.bn;
-  const SmemPlan plan = smem_plan(CBLK, b_rows, a_rows, a_stages, g.stages);
+  const SmemPlan plan = smem_plan(CBLK, b_rows, a_rows, a_stages, g.stages, GATHER);
   uint8_t *a_ring = smem + plan.a_off;
   uint8_t *b_ring = smem + plan.b_off;
   int4 *staging = reinterpret_cast<int4 *>(smem + plan.stage_off);
@@ -259,7 +401,8 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < g.stages; ++i) {
-      mbar_init(&b_full[i], 1);
+      // GATHER: the filter load's arrival plus one per gather lane.
+      mbar_init(&b_full[i], GATHER ? 33 : 1);
       mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -269,7 +412,7 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
     }
     mbar_init(drain, 1);
     fence_mbar_init();
-    tma_prefetch_desc(&tmap_x);
+    if constexpr (!GATHER) tma_prefetch_desc(&tmap_x);
     tma_prefetch_desc(&tmap_w);
   }
   if (warp == 1) {
@@ -293,7 +436,11 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
   griddep_wait();
   griddep_launch_dependents();
 
-  if (warp == 0) {
+  if (warp == 0 && GATHER) {
+    gather_producer<CBLK>(g, x, &tmap_w, a_ring, b_ring, plan,
+                          reinterpret_cast<int4 *>(smem + plan.rows_off), b_full, b_empty, ctl,
+                          wctx, tile_first, tile_step, lane);
+  } else if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       Ring ra, rb;
@@ -829,8 +976,12 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   const int32_t out_w = (s.w + 2 * s.pad_w - s.dilation_w * (s.s - 1) - 1) / s.stride_w + 1;
   cblk = pick_cblk(s.c);
   g = ConvGeom{};
+  const bool gemm_rows = mode == kModeGeneric || mode == kModeGather;  // A rows = output pixels
   g.M = s.n * out_h * out_w;
   g.K = s.k;
+  g.H = s.h;
+  g.W = s.w;
+  g.C = s.c;
   g.P = out_h;
   g.Q = out_w;
   g.PQ = out_h * out_w;
@@ -846,8 +997,7 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   g.kblocks = s.r * s.s * g.cblocks;
   // Single CTAs of GENERIC may run narrower N tiles (i8c_generic_bn).
   const int bn_align = out_kind == kOutInt8VectC ? 32 : 16;
-  g.bn = mode == kModeGeneric && !pair ? i8c_generic_bn(&s, bn_align, slots)
-                                       : i8c_pick_bn(s.k, bn_align);
+  g.bn = gemm_rows && !pair ? i8c_generic_bn(&s, bn_align, slots) : i8c_pick_bn(s.k, bn_align);
   g.pair = pair ? 1 : 0;
   g.acc_stride = (g.bn + 31) / 32 * 32;
   g.tmem_cols = next_pow2(2 * g.acc_stride);
@@ -856,9 +1006,10 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   const int b_bytes = (pair ? g.bn / 2 : g.bn) * cblk;
   // Shared memory left for the rings: minus the base alignment slack (1 KB),
   // the staging buffer and its 1 KB alignment, and the barriers.
-  const int budget = kMaxSmem - 2048 - 512 - static_cast<int>(kEpilogueStaging);
+  const int budget = kMaxSmem - 2048 - 512 - static_cast<int>(kEpilogueStaging) -
+                     (mode == kModeGather ? static_cast<int>(kGatherRowTable) + 16 : 0);
   int64_t positions = g.M;
-  if (mode != kModeGeneric) {
+  if (!gemm_rows) {
     // Padded grid: STRIP pads the row only (Wp = Q + S - 1, out_h rows);
     // HALO pads both (Hp x Wp, every tap is a shift of one staged tile).
     const bool halo = mode == kModeHalo;
@@ -894,6 +1045,7 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
     g.stages = stages;
     g.a_stages = stages;
     g.a_rows = kBlockM;
+    g.gather_lag = stages - 1 < 3 ? stages - 1 : 3;
   }
   g.m_tiles = static_cast<int32_t>((positions + tile_rows - 1) / tile_rows);
   g.n_tiles = (s.k + g.bn - 1) / g.bn;
@@ -915,9 +1067,9 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   // the next N tile (columns >= K are clipped, columns of a neighbour are not).
   // int8 NHWC: rows of K bytes (K % 16 == 0), 32-column blocks.
   if (out_kind == kOutInt32)
-    g.tma_store = mode == kModeGeneric && s.k % 4 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
+    g.tma_store = gemm_rows && s.k % 4 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
   else if (out_kind == kOutInt8Nhwc)
-    g.tma_store = mode == kModeGeneric && s.k % 16 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
+    g.tma_store = gemm_rows && s.k % 16 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
   else
     g.tma_store = 0;
   return true;
@@ -929,13 +1081,18 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
                                 cudaStream_t stream) {
   DeviceInfo &dev = device_info();
   CUtensorMap maps[3];
-  constexpr bool SHIFT = MODE != kModeGeneric;
+  constexpr bool SHIFT = MODE == kModeStrip || MODE == kModeHalo;
+  constexpr bool GATHER = MODE == kModeGather;
   const int pixels = SHIFT ? g.strip_px : kBlockM;
   const int count_w = SHIFT ? g.Wp : g.Q;
   const int count_h = MODE == kModeHalo ? g.rows : g.P;
   const int b_rows = PAIR ? g.bn / 2 : g.bn;
-  int8conv_status st = activation_map_im2col(s, x, CBLK, pixels, count_w, count_h, &maps[0]);
-  if (st != INT8CONV_OK) return st;
+  int8conv_status st = INT8CONV_OK;
+  maps[0] = CUtensorMap{};  // GATHER reads the activations through `x`
+  if (!GATHER) {
+    st = activation_map_im2col(s, x, CBLK, pixels, count_w, count_h, &maps[0]);
+    if (st != INT8CONV_OK) return st;
+  }
   st = filter_map_tiled(s, w, CBLK, b_rows, &maps[1]);
   if (st != INT8CONV_OK) return st;
   maps[2] = CUtensorMap{};
@@ -944,7 +1101,8 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
              : output_map_tiled(static_cast<int32_t *>(y), g.M, g.K, &maps[2]);
     if (st != INT8CONV_OK) return st;
   }
-  const SmemPlan plan = smem_plan(CBLK, b_rows, SHIFT ? g.a_rows : kBlockM, g.a_stages, g.stages);
+  const SmemPlan plan =
+      smem_plan(CBLK, b_rows, SHIFT ? g.a_rows : kBlockM, g.a_stages, g.stages, GATHER);
   auto kernel = conv_kernel<CBLK, MODE, PAIR, REQ>;
   // At least half an SM's shared memory: one CTA per SM, so a CTA never waits
   // for another's TMEM columns.
@@ -965,7 +1123,7 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   lp.block = dim3(kernel_threads<REQ>(), 1, 1);
   lp.smem = smem_bytes;
   lp.cluster = PAIR ? 2 : 1;
-  plan_args(lp, maps[0], maps[1], maps[2], g, b, static_cast<int32_t *>(y), RunCtl{}, rq);
+  plan_args(lp, maps[0], maps[1], maps[2], g, x, b, static_cast<int32_t *>(y), RunCtl{}, rq);
   return launch_plan(lp, stream);
 }
 
@@ -992,7 +1150,7 @@ static int8conv_status launch_cblk(const int8conv_shape &s, const ConvGeom &g, i
 // expand: 24 vs 27 us).
 static bool use_pair(const int8conv_shape &s, int mode, int out_kind) {
   const int pairing = pairing_mode();
-  if (pairing == 1) return false;
+  if (pairing == 1 || mode == kModeGather) return false;  // the gather warp feeds one CTA
   ConvGeom g;
   int cblk = 0;
   if (!plan_geometry(s, mode, true, out_kind, device_info().sm_count / 2, g, cblk)) return false;
@@ -1009,16 +1167,22 @@ static int8conv_status launch_mode(const int8conv_shape &s, const int8_t *x, con
   ConvGeom g;
   int cblk = 0;
   const int sms = device_info().sm_count;
-  if (use_pair(s, MODE, out_kind)) {
-    if (!plan_geometry(s, MODE, true, out_kind, sms / 2, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
-    return launch_cblk<MODE, true, REQ>(s, g, cblk, x, w, b, y, rq, stream);
+  if constexpr (MODE != kModeGather) {
+    if (use_pair(s, MODE, out_kind)) {
+      if (!plan_geometry(s, MODE, true, out_kind, sms / 2, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
+      return launch_cblk<MODE, true, REQ>(s, g, cblk, x, w, b, y, rq, stream);
+    }
   }
   if (!plan_geometry(s, MODE, false, out_kind, sms, g, cblk)) return INT8CONV_NOT_ELIGIBLE;
   return launch_cblk<MODE, false, REQ>(s, g, cblk, x, w, b, y, rq, stream);
 }
 
+// GENERIC stages the activations through the im2col tensor map where it can
+// be encoded, else with the gather warp (same tiles, same MMA and epilogue).
 int8conv_status launch_generic_impl(const int8conv_shape &s, const int8_t *x, const int8_t *w,
                                     const int32_t *b, int32_t *y, cudaStream_t stream) {
+  if (!i8c_im2col_ok(&s) || staging_mode() == 1)
+    return launch_mode<kModeGather, false>(s, x, w, b, y, Requant{}, kOutInt32, stream);
   return launch_mode<kModeGeneric, false>(s, x, w, b, y, Requant{}, kOutInt32, stream);
 }
 
@@ -1038,6 +1202,8 @@ int8conv_status launch_conv_requant(int strategy, const int8conv_shape &s, const
   const int out_kind = rq.layout == 1 ? kOutInt8VectC : kOutInt8Nhwc;
   switch (strategy) {
     case INT8CONV_GENERIC:
+      if (!i8c_im2col_ok(&s) || staging_mode() == 1)
+        return launch_mode<kModeGather, true>(s, x, w, b, y, rq, out_kind, stream);
       return launch_mode<kModeGeneric, true>(s, x, w, b, y, rq, out_kind, stream);
     case INT8CONV_STRIP:
       return launch_mode<kModeStrip, true>(s, x, w, b, y, rq, out_kind, stream);

@@ -20,6 +20,7 @@ std::atomic<uint64_t> g_wait_limit_ns{2000000000ull};
 std::atomic<uint32_t> g_starve{0};
 std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_pairing{0};
+std::atomic<int> g_staging{0};
 
 namespace {
 
@@ -199,6 +200,8 @@ int8conv_status launch_plan(LaunchPlan &plan, cudaStream_t stream) {
 }
 
 int pairing_mode() { return g_pairing.load(std::memory_order_relaxed); }
+
+int staging_mode() { return g_staging.load(std::memory_order_relaxed); }
 
 bool ensure_smem_attr(const void *kernel, int bytes) {
   // Remember the largest limit already set per (device, kernel).

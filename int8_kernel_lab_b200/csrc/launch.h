@@ -37,6 +37,9 @@ void note_launch();
 // CTA pairing policy: 0 auto, 1 single CTAs only, 2 pairs whenever possible.
 int pairing_mode();
 
+// GENERIC activation staging: 0 auto (im2col map where encodable), 1 gather.
+int staging_mode();
+
 // Sets the dynamic shared-memory limit of `kernel` once per device.
 bool ensure_smem_attr(const void *kernel, int bytes);
 

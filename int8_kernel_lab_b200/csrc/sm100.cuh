@@ -136,6 +136,23 @@ __device__ __forceinline__ void tma_load_im2col_4d(void *dst, const CUtensorMap 
       : "memory");
 }
 
+// ---- per-thread asynchronous copies (gather staging) ---------------------------
+// 16 bytes global -> shared, cached in L2 only.  `src_bytes` = 0 reads nothing
+// and writes 16 zero bytes (padding taps, channels past C, rows past M).
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Waits until at most N of this thread's committed copy groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---- TMA store (shared -> global) ------------------------------------------
 // Generic-proxy writes to shared memory must be fenced before an async-proxy
 // (TMA) read of the same bytes.

@@ -3,6 +3,8 @@
 
 Run where the reference sources exist (the GPU box has none):
     python tests/golden/make_golden.py [--reference PATH_TO_INT8_KERNEL_LAB]
+The reference checkout defaults to $INT8_KERNEL_LAB_REFERENCE, else a
+directory named `reference` beside this repository.
 
 For every row of golden_cases.csv it builds oracle/_ref/ref_<case> with
 oracle/Makefile (the reference's src/conv_lab.cu compiled unchanged, its
@@ -53,7 +55,8 @@ def inputs(name, shape, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("INT8_KERNEL_LAB_REFERENCE",
+                                                          str(ROOT.parent / "reference")))
     args = ap.parse_args()
     table = HERE / "golden_cases.csv"
     rows = list(csv.DictReader(open(table, newline="")))

@@ -20,12 +20,19 @@ static_assert(Smoke::out_h == 16 && Smoke::gemm_k == 288, "conv_shape formulas")
 static_assert(kSpatialStripEligible<BigStrip>, "reference strip shape stays eligible");
 static_assert(kSpatialStripEligible<Smoke>, "B200 strip needs no out_w % 128");
 static_assert(!kSpatialStripEligible<Down>, "stride_w 2 is not strip");
+// Beyond the TMA im2col limits (stride 16, pad 130): still launch_generic
+// shapes, as in the reference (gather staging).
+using Patch16 = ConvShape<8, 224, 224, 16, 768, 16, 16, 0, 0, 16, 16, 1, 1>;
+using Pad130 = ConvShape<1, 5, 5, 16, 8, 3, 3, 130, 130, 1, 1, 1, 1>;
+static_assert(!kSpatialStripEligible<Patch16>, "stride 16 is not strip");
 
 int main() {
   int status = 0;
   // Same call sites as src/conv_lab.cu:172-176 / :200-201 (null buffers: no GPU needed).
   if (launch_generic<Smoke>(nullptr, nullptr, nullptr, nullptr) != INT8CONV_BAD_POINTER) status = 1;
   if (launch_generic_sm80<Smoke>(nullptr, nullptr, nullptr, nullptr, 0) != INT8CONV_BAD_POINTER) status = 2;
+  if (launch_generic<Patch16>(nullptr, nullptr, nullptr, nullptr) != INT8CONV_BAD_POINTER) status = 4;
+  if (launch_generic_sm80<Pad130>(nullptr, nullptr, nullptr, nullptr) != INT8CONV_BAD_POINTER) status = 5;
   if constexpr (kSpatialStripEligible<BigStrip>) {
     if (launch_spatial_strip<BigStrip>(nullptr, nullptr, nullptr, nullptr) != INT8CONV_BAD_POINTER) status = 3;
   }

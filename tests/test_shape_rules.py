@@ -1,6 +1,7 @@
 """Eligibility predicates and the workloads table (host only)."""
 from pathlib import Path
 
+import numpy as np
 import pytest
 
 import int8_kernel_lab_b200 as m
@@ -167,3 +168,63 @@ def test_tail_split_and_narrow_tile_rules(tmp_path):
     assert list(map(int, lines[1].split())) == [32, 128, 128, 112, 64]
     # K = 700: three equal tiles of ceil(700 / 3) = 234 -> 240 columns.
     assert list(map(int, lines[2].split())) == [112, 128, 240]
+
+
+def im2col_encodable(s):
+    """Restatement of i8c_im2col_ok (include/int8conv_rules.h): the TMA im2col
+    tensor map's limits on pads, traversal strides, tap offsets and the
+    bounding-box corners of a 4-D map."""
+    def corner(extent, pad, stride, count):
+        return -pad + (count - 1) * stride + 1 - extent
+    return (s.valid and s.pad_h <= 127 and s.pad_w <= 127 and s.stride_h <= 8 and s.stride_w <= 8
+            and (s.r - 1) * s.dilation_h <= 127 and (s.s - 1) * s.dilation_w <= 127
+            and -128 <= corner(s.w, s.pad_w, s.stride_w, s.out_w) <= 127
+            and -128 <= corner(s.h, s.pad_h, s.stride_h, s.out_h) <= 127)
+
+
+# Shapes the reference's generic kernel computes (conv_shape.cuh:34-35 are its
+# only conditions) that lie beyond the im2col map: patch embeds, strides past 8,
+# a pad past 127, a tap span past 127.
+BEYOND_IM2COL = {
+    "patch16_s16": m.ConvShape(8, 224, 224, 16, 768, 16, 16, 0, 0, 16, 16, 1, 1),
+    "patch32_s32": m.ConvShape(2, 448, 448, 16, 256, 32, 32, 0, 0, 32, 32, 1, 1),
+    "stride9": m.ConvShape(2, 20, 20, 32, 16, 3, 3, 1, 1, 9, 9, 1, 1),
+    "stride12": m.ConvShape(1, 25, 30, 16, 12, 2, 3, 0, 1, 12, 12, 1, 1),
+    "pad130": m.ConvShape(1, 5, 5, 16, 8, 3, 3, 130, 130, 1, 1, 1, 1),
+    "span140": m.ConvShape(1, 150, 145, 16, 8, 3, 2, 1, 1, 2, 2, 70, 140),
+    # every parameter within its own limit, but the bounding box's upper
+    # corner (1 - 135 = -134) is past the map's range
+    "corner_only": m.ConvShape(1, 16, 135, 16, 8, 1, 2, 0, 0, 1, 8, 1, 127),
+}
+
+
+@pytest.mark.parametrize("name", sorted(BEYOND_IM2COL))
+def test_generic_takes_shapes_beyond_the_im2col_map(name):
+    s = BEYOND_IM2COL[name]
+    assert s.valid and not im2col_encodable(s), name
+    assert s.eligible("generic")
+    for fam in ("strip", "halo", "splitk"):  # these stage through the im2col map
+        assert not s.eligible(fam), (name, fam)
+    assert s.select() == "generic"
+
+
+def test_generic_eligible_is_shape_valid():
+    # GENERIC computes every valid shape, as the reference's generic does.
+    rng = np.random.RandomState(4)
+    seen_beyond = 0
+    for _ in range(3000):
+        s = m.ConvShape(
+            n=int(rng.randint(1, 5)), h=int(rng.randint(1, 300)), w=int(rng.randint(1, 300)),
+            c=int(rng.choice([8, 16, 48, 64, 200, 256])), k=int(rng.randint(1, 900)),
+            r=int(rng.randint(1, 40)), s=int(rng.randint(1, 40)),
+            pad_h=int(rng.randint(0, 300)), pad_w=int(rng.randint(0, 300)),
+            stride_h=int(rng.randint(1, 40)), stride_w=int(rng.randint(1, 40)),
+            dilation_h=int(rng.randint(1, 20)), dilation_w=int(rng.randint(1, 20)))
+        assert s.eligible("generic") == s.valid, s
+        if s.valid:
+            assert s.select() in ("generic", "splitk"), s
+            if not im2col_encodable(s):
+                seen_beyond += 1
+                assert s.select() == "generic"
+                assert not (s.eligible("strip") or s.eligible("halo") or s.eligible("splitk"))
+    assert seen_beyond > 100
