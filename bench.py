@@ -16,13 +16,20 @@ Printed (rank 0, one JSON line):
   e2e       same metric through the public API with pinned host buffers:
             host->device copy of each step's input shard, filter and bias,
             the launch, and the device->host copy of the NHWK output
-  roofline  the conv kernel's achieved TOPS vs the INT8 dense peak
+  roofline  the conv kernel's achieved TOPS vs the B200 dense INT8 peak
+            (4.5 POPS), with 2x the measured bf16 cuBLAS burst as a second figure
+  sustained the same launches back to back for --sustained-seconds under the
+            power cap, with the clocks of that loop
   cpu_baseline  the CPU oracle on the host cores (N=1 only), on whole images
-            of the same workload; the GPU outputs of those images are compared
-            with it (bit-exact) and the result is reported as `verified`
+            of the same workload
+  verified  the timed launches' own output against the CPU oracle: at N=1
+            image 0 and the cpu_baseline images, at N>1 (NCCL gather to rank 0)
+            the first and last image of every rank's shard plus a seeded
+            sample; the host-buffer (e2e) output separately
 --impl reference times the reference's own CPU implementation of the path
 (reference_value of src/conv_lab.cu:39-66, built from the reference sources
-into oracle/_ref) on the host cores instead.
+into oracle/_ref) on the host cores instead; that arm loads nothing of this
+package (shapes and inputs are computed here in plain Python).
 """
 from __future__ import annotations
 
@@ -47,6 +54,13 @@ sys.path.insert(0, str(ROOT))
 METRIC = "INT8 conv TOPS & % of B200 INT8 tensor peak at 1/2/4/8 GPUs vs host-CPU oracle"
 DEFAULT_WORKLOAD = "cfg5a_stress_3x3"
 NOMINAL_INT8_TOPS = 4500.0
+WORKLOADS_CSV = ROOT / "int8_kernel_lab_b200" / "workloads.csv"
+REFERENCE_SEED = 20260925
+SHAPE_FIELDS = ("n", "h", "w", "c", "k", "r", "s", "pad_h", "pad_w", "stride_h", "stride_w",
+                "dilation_h", "dilation_w")
+# The same statement in both arms (the GPU arm's actual set count is under "run").
+L2_POLICY = ("inputs larger than L2: the GPU arm's input + output set is >= 2x the 126 MB L2, "
+             "or enough sets rotate that consecutive steps never share one")
 
 
 def parse_args():
@@ -65,6 +79,8 @@ def parse_args():
                     help="image groups the host-buffer path overlaps copies over")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--sustained-seconds", type=float, default=2.0,
+                    help="length of the back-to-back loop under the power cap (0: skip)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -73,29 +89,23 @@ def parse_args():
 # helpers
 # ---------------------------------------------------------------------------
 
-def sustained_peak():
-    """2x the measured sustained bf16 figure (seconds-long loop under the power cap)."""
+def int8_peak():
+    """Roofline denominator of the conv kernel: B200's dense INT8 tensor peak,
+    4.5 POPS nominal.  The int8 tensor pipe itself, measured on this pool with
+    back-to-back kind::i8 MMAs at 1965 MHz, gives 4586 TOPS (98 % of nominal),
+    so the nominal figure is the tighter of the two."""
+    return NOMINAL_INT8_TOPS, ("B200 dense INT8 nominal 4.5 POPS (the int8 tensor pipe "
+                               "measures 4586 TOPS at 1965 MHz on this pool)")
+
+
+def bf16_peaks():
+    """2x the measured cuBLAS bf16 dense figures of MEASURED_PEAKS.json (burst,
+    sustained): B200's dense INT8 rate is 2x its bf16 rate."""
     try:
         data = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-        return 2.0 * float(data["bf16_tflops_sustained"])
+        return 2.0 * float(data["bf16_tflops"]), 2.0 * float(data["bf16_tflops_sustained"])
     except (OSError, KeyError, ValueError):
-        return 2.0 * 1400.0
-
-
-def measured_peaks():
-    """INT8 dense peak used as the roofline denominator.
-
-    MEASURED_PEAKS.json (driver-written) holds a measured cuBLAS bf16 dense
-    throughput; B200's dense INT8 rate is twice its bf16 rate (4.5 vs 2.25
-    PFLOP/s nominal), so the INT8 denominator is 2x the measured bf16 burst
-    figure.  Without the file the pool's fallback (1.59 PFLOP/s bf16) is used.
-    """
-    path = ROOT / "MEASURED_PEAKS.json"
-    try:
-        data = json.loads(path.read_text())
-        return 2.0 * float(data["bf16_tflops"]), "2x measured bf16 cuBLAS burst (MEASURED_PEAKS.json)"
-    except (OSError, KeyError, ValueError):
-        return 2.0 * 1590.0, "2x fallback bf16 1.59 PFLOP/s"
+        return 2.0 * 1590.0, 2.0 * 1400.0
 
 
 class ClockSampler:
@@ -195,30 +205,63 @@ class ClockSampler:
                 "region_ms": round((t1 - t0) * 1e3, 3), "period_ms": self.PERIOD_MS}
 
 
-def shard(n: int, rank: int, world: int):
-    """Images [start, stop) of `rank` (int8_kernel_lab_b200.sharding)."""
-    from int8_kernel_lab_b200.sharding import shard_range
-    return shard_range(n, rank, world)
-
-
 # ---------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------
+
+class PlainShape:
+    """A workloads.csv row with the shape algebra of conv_shape.cuh:22-32 (C++
+    truncating division in out_h/out_w), for the reference arm, which loads
+    nothing of this package."""
+
+    def __init__(self, **fields):
+        for f in SHAPE_FIELDS:
+            setattr(self, f, int(fields[f]))
+        self.out_h = int((self.h + 2 * self.pad_h - self.dilation_h * (self.r - 1) - 1)
+                         / self.stride_h) + 1
+        self.out_w = int((self.w + 2 * self.pad_w - self.dilation_w * (self.s - 1) - 1)
+                         / self.stride_w) + 1
+        self.gemm_m = self.n * self.out_h * self.out_w
+        self.gemm_k = self.r * self.s * self.c
+        self.input_elements = self.n * self.h * self.w * self.c
+        self.filter_elements = self.k * self.r * self.s * self.c
+        self.output_elements = self.gemm_m * self.k
+        self.ops = 2 * self.gemm_m * self.k * self.gemm_k
+
+
+def plain_workload(name: str) -> PlainShape:
+    with open(WORKLOADS_CSV, newline="") as stream:
+        for row in csv.DictReader(stream):
+            if row["name"] == name:
+                return PlainShape(**row)
+    raise SystemExit(f"unknown workload {name}")
+
+
+def plain_inputs(shape: PlainShape, seed: int = REFERENCE_SEED):
+    """The benchmark's seeded inputs: the same MT19937 draws, in the same
+    order, as the GPU arm's make_inputs (int8 uniform [-128,127], bias uniform
+    [-65536,65536])."""
+    import numpy as np
+    rng = np.random.RandomState(seed)
+    x = rng.randint(-128, 128, size=shape.input_elements, dtype=np.int16).astype(np.int8)
+    w = rng.randint(-128, 128, size=shape.filter_elements, dtype=np.int16).astype(np.int8)
+    b = rng.randint(-65536, 65537, size=shape.k, dtype=np.int64).astype(np.int32)
+    return x, w, b
+
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0  # only rank 0 runs and prints the reference arm
-    import numpy as np
-
-    import int8_kernel_lab_b200 as m
     sys.path.insert(0, str(ROOT / "oracle"))
     import pyoracle  # noqa: E402  (test infrastructure: the reference leg only)
 
-    shape = m.load_workloads()[args.workload]
-    x, w, b = m.make_inputs(shape)
+    shape = plain_workload(args.workload)
+    if args.batch > 0:
+        shape = PlainShape(**dict({f: getattr(shape, f) for f in SHAPE_FIELDS}, n=args.batch))
+    x, w, b = plain_inputs(shape)
     threads = os.cpu_count() or 1
-    binary = pyoracle.ref_binary(args.workload)
+    binary = pyoracle.ref_binary(args.workload) if args.batch <= 0 else None
     rows_per_image = shape.out_h * shape.out_w
     # Size each step so warmup + steps fit in about two minutes.
     budget_s = 120.0 / max(1, args.steps + args.warmup)
@@ -259,6 +302,7 @@ def run_reference(args):
         "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": workload_config(shape, args, args.gpus),
+        "run": {"reference_binary": str(binary.relative_to(ROOT)) if binary else None},
         "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0,
@@ -278,6 +322,7 @@ def workload_config(shape, args, world):
         "ops_per_step": shape.ops,
         "parallelism": f"batch-sharded x{world} (no data-path collective)",
         "values": "int8 uniform [-128,127], bias int32 uniform [-65536,65536], seed 20260925",
+        "l2": L2_POLICY,
     }
 
 
@@ -310,7 +355,8 @@ def run_ours(args):
     full = m.load_workloads()[args.workload]
     if args.batch > 0:
         full = full.with_batch(args.batch)
-    lo, hi = shard(full.n, rank, world)
+    from int8_kernel_lab_b200.sharding import shard_range
+    lo, hi = shard_range(full.n, rank, world)
     local_shape = full.with_batch(hi - lo)
     x, w, b = m.make_inputs(full)
     per_image_in = full.h * full.w * full.c
@@ -347,7 +393,7 @@ def run_ours(args):
         torch.cuda.synchronize()
 
     gpu_uuid = "GPU-" + str(props.uuid) if hasattr(props, "uuid") else str(local)
-    sampler = ClockSampler(gpu_uuid) if rank == 0 else None
+    sampler = ClockSampler(gpu_uuid)  # every rank records its own GPU's clocks
     if sampler:
         sampler.wait_ready()
     for i in range(args.warmup):
@@ -378,14 +424,29 @@ def run_ours(args):
     value = full.ops / (ms_per_step * 1e-3) / 1e12
     local_launch_ms = elapsed_ms / args.steps  # one kernel per step on this stream
     achieved = local_shape.ops / (local_launch_ms * 1e-3) / 1e12
-    peak, peak_src = measured_peaks()
+    peak, peak_src = int8_peak()
+    bf16_burst, bf16_sustained = bf16_peaks()
+    # The last timed launch's output, kept aside for verification before any
+    # later launch reuses its buffer.
+    y_timed = dys[(args.steps - 1) % sets].clone()
+
+    # ---- the same launches back to back under the power cap ----
+    sustained = None
+    if args.sustained_seconds > 0:
+        sustained = sustained_loop(step, local_shape, full, args, stream, sampler_factory=(
+            (lambda: ClockSampler(gpu_uuid)) if rank == 0 else None), barrier=barrier,
+            dist=dist, bf16_sustained=bf16_sustained)
 
     # ---- end to end through the public API, host buffers ----
+    # Its own device buffers: the timed launches' output stays for verification.
     hx = torch.from_numpy(x_local).pin_memory()
     hw = torch.from_numpy(w).pin_memory()
     hb = torch.from_numpy(b).pin_memory()
     hy = torch.empty(local_shape.output_elements, dtype=torch.int32).pin_memory()
-    ex, ew, eb, ey = dxs[0], dw, db, dys[0]
+    ex = torch.empty_like(dxs[0])
+    ew = torch.empty_like(dw)
+    eb = torch.empty_like(db)
+    ey = torch.empty(local_shape.output_elements, dtype=torch.int32, device="cuda")
 
     chunks = max(1, min(args.e2e_chunks, local_shape.n))
 
@@ -409,16 +470,17 @@ def run_ours(args):
     e2e_ms = float(te.item()) / args.e2e_steps
     h2d = int(hx.numel() + hw.numel() + 4 * hb.numel()) * world
     d2h = int(4 * hy.numel()) * world
+    if m.device_status() != _abi.OK:
+        raise SystemExit("device status not OK after the end-to-end steps")
 
-    # ---- verification / CPU baseline ----
-    y_local = hy.numpy()  # output of the last e2e step (identical inputs)
+    # ---- verification against the CPU oracle / CPU baseline ----
     cpu = None
-    verify = None
-    if world == 1 and not args.no_cpu_baseline and rank == 0:
-        cpu = cpu_baseline(full, x, w, b, y_local, args)
-    elif dist is not None:
-        verify = verify_sharded(full, dxs, dys, dw, db, local_shape, x, strategy, dist, rank,
-                                world, lo, hi)
+    verified = None
+    if world == 1:
+        if rank == 0:
+            cpu, verified = verify_single(full, x, w, b, y_timed.cpu().numpy(), hy.numpy(), args)
+    else:
+        verified = verify_sharded(full, x, w, b, y_timed, hy, dist, rank, world, clocks)
 
     if rank == 0:
         line = {
@@ -426,33 +488,83 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8", "data": "synthetic",
-            "config": dict(workload_config(full, args, world), strategy=strategy,
-                           images_per_rank=hi - lo,
-                           l2=("inputs larger than L2: %d rotating input/output set(s), "
-                               "%.0f MB per set, L2 %.0f MB" % (sets, per_set / 1e6, l2 / 1e6))),
+            "config": workload_config(full, args, world),
+            "run": {"strategy": strategy, "images_per_rank": hi - lo, "rotating_sets": sets,
+                    "set_mb": round(per_set / 1e6, 1), "l2_mb": round(l2 / 1e6, 1)},
             "e2e": {"value": full.ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "api": "int8conv_launch_host",
                     "chunks": chunks},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TOPS", "frac": achieved / peak, "peak_source": peak_src,
-                         "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
-                         "frac_of_sustained": achieved / sustained_peak(),
+                         "frac_of_2x_measured_bf16_burst": achieved / bf16_burst,
                          "kernel": f"conv_kernel ({strategy})",
-                         "launch_ms": local_launch_ms, "traffic": traffic_per_launch(args,
-                                                                                     local_shape)},
+                         "launch_ms": local_launch_ms,
+                         "traffic": traffic_per_launch(args, local_shape),
+                         "traffic_source": "DRAM bytes per launch from the committed ncu "
+                                           "capture profiles/traffic.json, scaled by images; "
+                                           "not measured in this run"},
             "gpu_launches": int(launches),
             "clocks": clocks,
+            "verified": verified,
         }
+        if sustained is not None:
+            line["sustained"] = sustained
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        if verify is not None:
-            line["verified_sharded_vs_single_gpu"] = verify
+        if world > 1 and verified is not None:
+            line["clocks_per_rank"] = verified.pop("clocks_per_rank")
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def sustained_loop(step, local_shape, full, args, stream, sampler_factory, barrier, dist,
+                   bf16_sustained):
+    """The timed launches back to back for about --sustained-seconds, long
+    enough for the 1 kW power cap to set the clock: TOPS and the clocks of
+    that loop, next to the burst figure of the main timed region."""
+    import torch
+
+    # Launches per second from a short probe, then one bracketed loop.
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(4):
+        step(i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    per_ms = max(t0.elapsed_time(t1) / 4, 1e-3)
+    n = torch.tensor([max(8, int(args.sustained_seconds * 1e3 / per_ms))], device="cuda")
+    if dist is not None:
+        dist.all_reduce(n, op=dist.ReduceOp.MAX)  # every rank runs the same count
+    n = int(n.item())
+    sampler = sampler_factory() if sampler_factory else None
+    if sampler:
+        sampler.wait_ready()
+    barrier()
+    if sampler:
+        sampler.mark_start()
+    t0.record(stream)
+    for i in range(n):
+        step(i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.mark_stop()
+    clocks = sampler.stop() if sampler else None
+    tt = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item()) / n
+    achieved = local_shape.ops / (t0.elapsed_time(t1) / n * 1e-3) / 1e12
+    return {"value": full.ops / (ms * 1e-3) / 1e12, "unit": "TOPS", "steps": n,
+            "seconds": round(float(tt.item()) / 1e3, 3), "ms_per_step": ms,
+            "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
+            "frac_of_2x_measured_bf16_sustained": achieved / bf16_sustained,
+            "clocks": clocks}
 
 
 def traffic_per_launch(args, local_shape):
@@ -466,9 +578,11 @@ def traffic_per_launch(args, local_shape):
         return None
 
 
-def cpu_baseline(shape, x, w, b, y_gpu, args):
-    """Times the oracle port (oracle/conv_oracle.c) on whole images of the
-    workload with all host threads and checks the GPU output of those images."""
+def verify_single(shape, x, w, b, y_timed, y_e2e, args):
+    """N = 1: times the oracle port (oracle/conv_oracle.c) on whole images of
+    the workload with all host threads (the cpu_baseline), and checks image 0
+    and those images of the timed launches' output and of the host-buffer
+    output against it, bit-exactly."""
     import numpy as np
     sys.path.insert(0, str(ROOT / "oracle"))
     import pyoracle  # noqa: E402  (test infrastructure: the cpu_baseline leg only)
@@ -479,37 +593,73 @@ def cpu_baseline(shape, x, w, b, y_gpu, args):
     t0 = time.perf_counter()
     first = pyoracle.conv_rows(shape, x, w, b, 0, rows, threads)
     t1 = time.perf_counter() - t0
-    images = int(max(1, min(shape.n - 1, args.cpu_seconds / max(t1, 1e-6) - 1)))
-    # images [n - images, n): the end of the batch, a different rank's shard at N>1
+    if args.no_cpu_baseline:
+        images = 0
+    else:
+        images = int(max(1, min(shape.n - 1, args.cpu_seconds / max(t1, 1e-6) - 1)))
+    # images [n - images, n): the end of the batch
     lo = shape.n - images
-    t0 = time.perf_counter()
-    tail = pyoracle.conv_rows(shape, x, w, b, lo * rows, shape.n * rows, threads)
-    sec = time.perf_counter() - t0
-    ops = 2.0 * images * rows * shape.k * shape.gemm_k
     k = shape.k
-    ok = bool(np.array_equal(y_gpu[:rows * k], first) and
-              np.array_equal(y_gpu[lo * rows * k:], tail))
-    return {"value": ops / sec / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
-            "sample": f"{images} whole image(s) of {args.workload} (images {lo}..{shape.n - 1}), "
-                      f"{ops / 1e9:.1f} Gop in {sec:.2f} s",
-            "verified": ok, "verified_images": f"0 and {lo}..{shape.n - 1}"}
+    ok_timed = bool(np.array_equal(y_timed[:rows * k], first))
+    ok_e2e = bool(np.array_equal(y_e2e[:rows * k], first))
+    cpu = None
+    if images > 0:
+        t0 = time.perf_counter()
+        tail = pyoracle.conv_rows(shape, x, w, b, lo * rows, shape.n * rows, threads)
+        sec = time.perf_counter() - t0
+        ops = 2.0 * images * rows * shape.k * shape.gemm_k
+        ok_timed = ok_timed and bool(np.array_equal(y_timed[lo * rows * k:], tail))
+        ok_e2e = ok_e2e and bool(np.array_equal(y_e2e[lo * rows * k:], tail))
+        cpu = {"value": ops / sec / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+               "sample": f"{images} whole image(s) of {args.workload} (images {lo}.."
+                         f"{shape.n - 1}), {ops / 1e9:.1f} Gop in {sec:.2f} s"}
+    verified = {"timed_output": ok_timed, "e2e_output": ok_e2e, "against": "CPU oracle",
+                "images": f"0 and {lo}..{shape.n - 1}" if images else "0"}
+    return cpu, verified
 
 
-def verify_sharded(full, dxs, dys, dw, db, local_shape, x, strategy, dist, rank, world, lo, hi):
-    """NCCL gathers every rank's NHWK slice to rank 0, which recomputes the
-    whole batch on its own GPU and compares bit-exactly (outside timing)."""
+def verify_sharded(full, x, w, b, y_timed, y_e2e, dist, rank, world, clocks):
+    """N > 1: NCCL gathers every rank's NHWK slice of the timed launches'
+    output (and of the host-buffer output) to rank 0, which checks the first
+    and last image of every rank's shard plus a seeded sample of all outputs
+    against the CPU oracle, bit-exactly (outside the timed region).  Rank 0
+    also collects every rank's clock record."""
+    import numpy as np
     import torch
 
-    import int8_kernel_lab_b200 as m
-    from int8_kernel_lab_b200.sharding import gather_outputs
-    gathered = gather_outputs(dys[0], full, rank, world, dist)
+    from int8_kernel_lab_b200.sharding import gather_outputs, shard_range
+    gathered = gather_outputs(y_timed, full, rank, world, dist)
+    gathered_e2e = gather_outputs(y_e2e.cuda(), full, rank, world, dist)
+    records = [None] * world
+    dist.all_gather_object(records, clocks)
     if rank != 0:
         return None
-    xall = torch.from_numpy(x).cuda()
-    yall = torch.empty(full.output_elements, dtype=torch.int32, device="cuda")
-    m.launch(strategy if full.eligible(strategy) else "generic", full, xall, dw, db, yall)
-    torch.cuda.synchronize()
-    return bool(torch.equal(gathered, yall))
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pyoracle  # noqa: E402  (test infrastructure: the verification leg only)
+
+    threads = os.cpu_count() or 1
+    y = gathered.cpu().numpy()
+    y2 = gathered_e2e.cpu().numpy()
+    rows = full.out_h * full.out_w
+    k = full.k
+    ok = ok2 = True
+    checked = []
+    for r in range(world):
+        lo, hi = shard_range(full.n, r, world)
+        for img in sorted({lo, hi - 1}):
+            want = pyoracle.conv_rows(full, x, w, b, img * rows, (img + 1) * rows, threads)
+            span = slice(img * rows * k, (img + 1) * rows * k)
+            ok = ok and bool(np.array_equal(y[span], want))
+            ok2 = ok2 and bool(np.array_equal(y2[span], want))
+            checked.append(img)
+    rng = np.random.RandomState(world)
+    idx = rng.randint(0, full.output_elements, size=200_000, dtype=np.int64)
+    want = pyoracle.values(full, x, w, b, idx, threads)
+    ok = ok and bool(np.array_equal(y[idx], want))
+    ok2 = ok2 and bool(np.array_equal(y2[idx], want))
+    return {"timed_output": ok, "e2e_output": ok2, "against": "CPU oracle",
+            "images": checked, "sampled_outputs": int(idx.size),
+            "clocks_per_rank": records}
 
 
 def main():

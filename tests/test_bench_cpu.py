@@ -105,3 +105,54 @@ def test_reference_arm_other_ranks_exit_quietly():
                                  "--warmup", "0"], {"RANK": "1", "WORLD_SIZE": "2"})
     assert rc == 0, err
     assert lines == []
+
+
+SHAPE_ATTRS = ("n", "h", "w", "c", "k", "r", "s", "pad_h", "pad_w", "stride_h", "stride_w",
+               "dilation_h", "dilation_w", "out_h", "out_w", "gemm_m", "gemm_k",
+               "input_elements", "filter_elements", "output_elements", "ops")
+
+
+def test_plain_shapes_and_inputs_match_the_package():
+    # The reference arm computes shapes and inputs without this package; they
+    # must be the GPU arm's, field for field and byte for byte.
+    import numpy as np
+
+    import int8_kernel_lab_b200 as m
+    for name, s in m.load_workloads().items():
+        p = bench.plain_workload(name)
+        for a in SHAPE_ATTRS:
+            assert getattr(p, a) == getattr(s, a), (name, a)
+    for name in ("cfg4c_tail_k100", "g_like", "cfg1_smoke"):
+        s = m.load_workloads().get(name) or m.ConvShape(2, 9, 7, 16, 24, 3, 3, 1, 1, 2, 2, 1, 1)
+        p = bench.PlainShape(**{f: getattr(s, f) for f in bench.SHAPE_FIELDS})
+        for got, want in zip(bench.plain_inputs(p), m.make_inputs(s)):
+            assert got.dtype == want.dtype and np.array_equal(got, want), name
+
+
+def test_both_arms_emit_the_same_config():
+    import argparse
+
+    import int8_kernel_lab_b200 as m
+    args = argparse.Namespace(workload="cfg5a_stress_3x3")
+    for world in (1, 8):
+        ours = bench.workload_config(m.load_workloads()[args.workload], args, world)
+        ref = bench.workload_config(bench.plain_workload(args.workload), args, world)
+        assert ours == ref
+
+
+def test_reference_arm_loads_nothing_of_the_package():
+    import subprocess
+    probe = (
+        "import runpy, sys\n"
+        "sys.argv = ['bench.py', '--impl', 'reference', '--workload', 'cfg1_smoke',"
+        " '--steps', '1', '--warmup', '0']\n"
+        "try:\n"
+        "    runpy.run_path('bench.py', run_name='__main__')\n"
+        "except SystemExit as e:\n"
+        "    assert not e.code, e.code\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "print('PKG', 'int8_kernel_lab_b200' in sys.modules, 'libint8conv' in maps)\n")
+    out = subprocess.run([sys.executable, "-c", probe], capture_output=True, text=True,
+                         cwd=str(ROOT), timeout=600)
+    assert out.returncode == 0, out.stderr
+    assert "PKG False False" in out.stdout
