@@ -13,7 +13,10 @@
 //     the appended ones: eligible_halo, eligible_splitk, halo_ms, splitk_ms,
 //     halo_correct, splitk_correct, gpus, tops, roofline_frac, oracle_ms,
 //     oracle_threads, graph_ms, selected (the family int8conv_select picks),
-//     epilogue.
+//     epilogue, l2 ("warm", or "rotated:<sets>" with --rotate-l2).
+// --rotate-l2 times every launch on the next of enough input/output sets
+// that together span twice the L2, so memory-bound shapes are timed L2-cold
+// (the reference times one buffer set, L2-warm for small shapes).
 // --epilogue int8 | int8x32 times int8conv_launch_requant (NHWC or cuDNN's
 // NCHW_VECT_C int8 output) with seeded per-channel multipliers and exponents.
 // Validation compares EVERY output element (the reference checks 2048
@@ -34,8 +37,10 @@
 #include <functional>
 #include <iomanip>
 #include <iostream>
+#include <memory>
 #include <random>
 #include <sstream>
+#include <stdexcept>
 #include <string>
 #include <thread>
 #include <vector>
@@ -45,27 +50,30 @@
 
 namespace {
 
+// A failed CUDA runtime call ends the run (exit code 1, the call named).
+struct CudaFailure : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
 void check(cudaError_t status, const char *what) {
-  if (status != cudaSuccess) {
-    std::cerr << what << ": " << cudaGetErrorString(status) << '\n';
-    std::exit(EXIT_FAILURE);
-  }
+  if (status == cudaSuccess) return;
+  throw CudaFailure(std::string(what) + ": " + cudaGetErrorString(status));
 }
 
-template <class T>
-class DeviceBuffer {
- public:
-  explicit DeviceBuffer(size_t elements) {
-    check(cudaMalloc(&data_, std::max<size_t>(elements, 1) * sizeof(T)), "cudaMalloc");
-  }
-  ~DeviceBuffer() { cudaFree(data_); }
-  T *get() { return data_; }
-  DeviceBuffer(const DeviceBuffer &) = delete;
-  DeviceBuffer &operator=(const DeviceBuffer &) = delete;
-
- private:
-  T *data_ = nullptr;
+// Device array of `count` T (at least one element, so an empty tensor still
+// has a valid, aligned address), freed with its owner.
+struct CudaFree {
+  void operator()(void *p) const { cudaFree(p); }
 };
+template <class T>
+using DeviceArray = std::unique_ptr<T, CudaFree>;
+
+template <class T>
+DeviceArray<T> device_array(size_t count) {
+  void *p = nullptr;
+  check(cudaMalloc(&p, (count == 0 ? 1 : count) * sizeof(T)), "cudaMalloc");
+  return DeviceArray<T>(static_cast<T *>(p));
+}
 
 struct Options {
   std::string strategy = "both";
@@ -82,6 +90,7 @@ struct Options {
   int pairing = 0;
   long long validate_samples = 0;  // 0: every output
   std::string epilogue = "int32";  // int32 | int8 (NHWC) | int8x32 (NCHW_VECT_C)
+  bool rotate_l2 = false;          // time over rotating buffer sets (L2-cold)
 };
 
 [[noreturn]] void usage() {
@@ -89,7 +98,7 @@ struct Options {
                "[--warmup N] [--iterations N] [--case NAME] [--config CSV] "
                "[--values full|reference] [--seed S] [--batch N] [--peak-tops T] "
                "[--no-graph] [--pairing auto|single|pair] [--validate-samples N] "
-               "[--epilogue int32|int8|int8x32]\n";
+               "[--epilogue int32|int8|int8x32] [--rotate-l2]\n";
   std::exit(EXIT_FAILURE);
 }
 
@@ -103,6 +112,7 @@ Options parse_options(int argc, char **argv) {
     };
     if (arg == "--csv") o.csv = true;
     else if (arg == "--no-graph") o.graph = false;
+    else if (arg == "--rotate-l2") o.rotate_l2 = true;
     else if (arg == "--strategy") o.strategy = value();
     else if (arg == "--warmup") o.warmup = std::stoi(value());
     else if (arg == "--iterations") o.iterations = std::stoi(value());
@@ -249,31 +259,32 @@ bool validate_all(const int8conv_shape &s, const int8conv_dims &d,
   return true;
 }
 
+// Per-launch device time, the reference's method (src/conv_lab.cu:88-110):
+// `warmup` untimed launches, then `iterations` launches each bracketed by its
+// own pair of events and completed before the next starts; the median.
+// `launch(i)` runs the i-th timed launch (the buffer set it uses may rotate).
 template <class Function>
-float measure(Function launch, int warmup, int iterations) {
-  for (int i = 0; i < warmup; ++i) launch();
-  check(cudaDeviceSynchronize(), "warmup");
-  std::vector<float> samples;
-  samples.reserve(iterations);
-  cudaEvent_t start, stop;
-  check(cudaEventCreate(&start), "cudaEventCreate start");
-  check(cudaEventCreate(&stop), "cudaEventCreate stop");
+float median_launch_ms(Function launch, int warmup, int iterations) {
+  for (int i = 0; i < warmup; ++i) launch(i);
+  check(cudaDeviceSynchronize(), "warm-up launches");
+  std::vector<cudaEvent_t> marks(2 * static_cast<size_t>(iterations));
+  for (auto &e : marks) check(cudaEventCreate(&e), "cudaEventCreate");
   for (int i = 0; i < iterations; ++i) {
-    check(cudaEventRecord(start), "cudaEventRecord start");
-    launch();
-    check(cudaEventRecord(stop), "cudaEventRecord stop");
-    check(cudaEventSynchronize(stop), "cudaEventSynchronize");
-    float ms = 0;
-    check(cudaEventElapsedTime(&ms, start, stop), "cudaEventElapsedTime");
-    samples.push_back(ms);
+    check(cudaEventRecord(marks[2 * i]), "cudaEventRecord");
+    launch(warmup + i);
+    check(cudaEventRecord(marks[2 * i + 1]), "cudaEventRecord");
+    check(cudaEventSynchronize(marks[2 * i + 1]), "cudaEventSynchronize");
   }
-  cudaEventDestroy(start);
-  cudaEventDestroy(stop);
-  std::sort(samples.begin(), samples.end());
-  return samples[samples.size() / 2];
+  std::vector<float> times(iterations);
+  for (int i = 0; i < iterations; ++i)
+    check(cudaEventElapsedTime(&times[i], marks[2 * i], marks[2 * i + 1]), "elapsed time");
+  for (auto e : marks) cudaEventDestroy(e);
+  std::nth_element(times.begin(), times.begin() + iterations / 2, times.end());
+  return times[iterations / 2];
 }
 
-// Launch time amortised over a CUDA graph of `count` back-to-back launches.
+// Launch time amortised over a CUDA graph of `count` back-to-back launches
+// (launch(stream, i): the i-th, whose buffer set may rotate).
 template <class Function>
 float measure_graph(Function launch, int count, int replays) {
   cudaStream_t stream;
@@ -281,7 +292,7 @@ float measure_graph(Function launch, int count, int replays) {
   cudaGraph_t graph;
   cudaGraphExec_t exec;
   check(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "capture");
-  for (int i = 0; i < count; ++i) launch(stream);
+  for (int i = 0; i < count; ++i) launch(stream, i);
   check(cudaStreamEndCapture(stream, &graph), "end capture");
   check(cudaGraphInstantiate(&exec, graph, 0), "instantiate");
   check(cudaGraphLaunch(exec, stream), "graph warmup");
@@ -314,9 +325,7 @@ std::string fmt(double v) {
   return os.str();
 }
 
-}  // namespace
-
-int main(int argc, char **argv) {
+int run_lab(int argc, char **argv) {
   Options parsed;
   try {
     parsed = parse_options(argc, argv);
@@ -361,12 +370,33 @@ int main(int argc, char **argv) {
   for (auto &v : multiplier) v = mult_values(rng);
   for (auto &v : exponent) v = exp_values(rng);
 
-  DeviceBuffer<int8_t> d_input(input.size());
-  DeviceBuffer<int8_t> d_filter(filter.size());
-  DeviceBuffer<int32_t> d_bias(bias.size());
-  DeviceBuffer<int32_t> d_output(int8_out ? 1 : d.output_elements);
-  DeviceBuffer<int8_t> d_output8(int8_out ? d.output_elements : 1);
-  DeviceBuffer<int32_t> d_multiplier(shape.k), d_exponent(shape.k);
+  // Input/output sets: one, or with --rotate-l2 enough that consecutive timed
+  // launches never find their operands in L2 (the sets together span at
+  // least twice the L2 size); every set holds the same input.
+  const size_t out_bytes = static_cast<size_t>(d.output_elements) * (int8_out ? 1 : 4);
+  const size_t set_bytes = input.size() + out_bytes;
+  int l2_bytes = 0;
+  {
+    int dev = 0;
+    check(cudaGetDevice(&dev), "cudaGetDevice");
+    check(cudaDeviceGetAttribute(&l2_bytes, cudaDevAttrL2CacheSize, dev), "L2 size");
+  }
+  const int sets = options.rotate_l2 && set_bytes < 2 * static_cast<size_t>(l2_bytes)
+                       ? static_cast<int>((2 * static_cast<size_t>(l2_bytes) + set_bytes - 1) /
+                                          set_bytes)
+                       : 1;
+  std::vector<DeviceArray<int8_t>> d_inputs;
+  std::vector<DeviceArray<int32_t>> d_outputs;
+  std::vector<DeviceArray<int8_t>> d_outputs8;
+  for (int i = 0; i < sets; ++i) {
+    d_inputs.push_back(device_array<int8_t>(input.size()));
+    d_outputs.push_back(device_array<int32_t>(int8_out ? 1 : d.output_elements));
+    d_outputs8.push_back(device_array<int8_t>(int8_out ? d.output_elements : 1));
+  }
+  auto d_filter = device_array<int8_t>(filter.size());
+  auto d_bias = device_array<int32_t>(bias.size());
+  auto d_multiplier = device_array<int32_t>(shape.k);
+  auto d_exponent = device_array<int32_t>(shape.k);
   check(cudaMemcpy(d_multiplier.get(), multiplier.data(), shape.k * sizeof(int32_t),
                    cudaMemcpyHostToDevice),
         "copy multipliers");
@@ -377,7 +407,9 @@ int main(int argc, char **argv) {
   auto expect = [&](int32_t v, int k) -> int32_t {
     return int8_out ? i8c::rq_apply(v, multiplier[k], exponent[k], 0, false) : v;
   };
-  check(cudaMemcpy(d_input.get(), input.data(), input.size(), cudaMemcpyHostToDevice), "copy input");
+  for (auto &d_input : d_inputs)
+    check(cudaMemcpy(d_input.get(), input.data(), input.size(), cudaMemcpyHostToDevice),
+          "copy input");
   check(cudaMemcpy(d_filter.get(), filter.data(), filter.size(), cudaMemcpyHostToDevice),
         "copy filter");
   check(cudaMemcpy(d_bias.get(), bias.data(), bias.size() * sizeof(int32_t),
@@ -407,26 +439,29 @@ int main(int argc, char **argv) {
     correct[f] = true;
     if (!run[f] || !eligible[f]) continue;
     const size_t ws_bytes = int8conv_workspace_bytes(&shape, f);
-    DeviceBuffer<uint8_t> workspace(ws_bytes);
-    auto launch_on = [&](cudaStream_t stream) {
+    auto workspace = device_array<uint8_t>(ws_bytes);
+    // Launch number i uses buffer set i % sets.
+    auto launch_on = [&](cudaStream_t stream, int i) {
+      const int set = i % sets;
       const int8conv_status st =
-          int8_out ? int8conv_launch_requant(f, &shape, d_input.get(), d_filter.get(),
-                                             d_bias.get(), &requant, d_output8.get(),
+          int8_out ? int8conv_launch_requant(f, &shape, d_inputs[set].get(), d_filter.get(),
+                                             d_bias.get(), &requant, d_outputs8[set].get(),
                                              workspace.get(), ws_bytes, stream)
-                   : int8conv_launch(f, &shape, d_input.get(), d_filter.get(), d_bias.get(),
-                                     d_output.get(), workspace.get(), ws_bytes, stream);
+                   : int8conv_launch(f, &shape, d_inputs[set].get(), d_filter.get(),
+                                     d_bias.get(), d_outputs[set].get(), workspace.get(),
+                                     ws_bytes, stream);
       if (st != INT8CONV_OK) {
         std::cerr << int8conv_strategy_name(f) << " launch: " << int8conv_status_string(st)
                   << '\n';
         std::exit(EXIT_FAILURE);
       }
     };
-    auto launch = [&] { launch_on(nullptr); };
+    auto launch = [&](int i) { launch_on(nullptr, i); };
     if (int8_out)
-      check(cudaMemset(d_output8.get(), 0xA5, d.output_elements), "poison");
+      check(cudaMemset(d_outputs8[0].get(), 0xA5, d.output_elements), "poison");
     else
-      check(cudaMemset(d_output.get(), 0xA5, d.output_elements * sizeof(int32_t)), "poison");
-    launch();
+      check(cudaMemset(d_outputs[0].get(), 0xA5, d.output_elements * sizeof(int32_t)), "poison");
+    launch(0);
     check(cudaGetLastError(), "launch");
     check(cudaDeviceSynchronize(), "synchronize");
     if (int8conv_device_status() != INT8CONV_OK) {
@@ -437,7 +472,7 @@ int main(int argc, char **argv) {
     if (int8_out) {
       // Back to NHWK order, widened, so one validator serves every epilogue.
       std::vector<int8_t> out8(d.output_elements);
-      check(cudaMemcpy(out8.data(), d_output8.get(), out8.size(), cudaMemcpyDeviceToHost),
+      check(cudaMemcpy(out8.data(), d_outputs8[0].get(), out8.size(), cudaMemcpyDeviceToHost),
             "copy output");
       const int64_t pq = static_cast<int64_t>(d.out_h) * d.out_w;
       for (int64_t i = 0; i < d.output_elements; ++i) {
@@ -450,7 +485,7 @@ int main(int argc, char **argv) {
         output[i] = out8[src];
       }
     } else {
-      check(cudaMemcpy(output.data(), d_output.get(), output.size() * sizeof(int32_t),
+      check(cudaMemcpy(output.data(), d_outputs[0].get(), output.size() * sizeof(int32_t),
                        cudaMemcpyDeviceToHost),
             "copy output");
     }
@@ -460,7 +495,7 @@ int main(int argc, char **argv) {
                               expect);
     oracle_ms = std::max(oracle_ms, vms);
     if (!correct[f]) continue;
-    ms[f] = measure(launch, options.warmup, options.iterations);
+    ms[f] = median_launch_ms(launch, options.warmup, options.iterations);
     if (options.graph) graph_ms[f] = measure_graph(launch_on, 20, 11);
   }
 
@@ -477,7 +512,7 @@ int main(int argc, char **argv) {
     std::cout << "case,n,h,w,c,k,r,s,out_h,out_w,eligible_strip,generic_ms,strip_ms,winner,"
                  "generic_correct,strip_correct,eligible_halo,eligible_splitk,halo_ms,splitk_ms,"
                  "halo_correct,splitk_correct,gpus,tops,roofline_frac,oracle_ms,oracle_threads,"
-                 "graph_ms,selected,epilogue\n";
+                 "graph_ms,selected,epilogue,l2\n";
     std::cout << options.case_name << ',' << shape.n << ',' << shape.h << ',' << shape.w << ','
               << shape.c << ',' << shape.k << ',' << shape.r << ',' << shape.s << ',' << d.out_h
               << ',' << d.out_w << ',' << (eligible[INT8CONV_STRIP] ? 1 : 0) << ','
@@ -490,6 +525,7 @@ int main(int argc, char **argv) {
               << fmt(tops < 0 ? -1.0 : tops / options.peak_tops) << ',' << fmt(oracle_ms) << ','
               << threads << ',' << (winner < 0 ? -1.0f : graph_ms[winner]) << ','
               << int8conv_strategy_name(int8conv_select(&shape)) << ',' << options.epilogue
+              << ',' << (options.rotate_l2 ? "rotated:" + std::to_string(sets) : std::string("warm"))
               << '\n';
   } else {
     std::cout << options.case_name << ":";
@@ -507,4 +543,15 @@ int main(int argc, char **argv) {
     std::cout << '\n';
   }
   return all_correct && winner >= 0 ? 0 : 1;
+}
+
+}  // namespace
+
+int main(int argc, char **argv) {
+  try {
+    return run_lab(argc, argv);
+  } catch (const CudaFailure &e) {
+    std::cerr << e.what() << '\n';
+    return EXIT_FAILURE;
+  }
 }

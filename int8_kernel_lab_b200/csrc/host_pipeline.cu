@@ -2,7 +2,10 @@
 // PCIe copies overlapped with compute.
 //
 // The batch is split into `chunks` groups of whole images (every image is an
-// independent convolution).  Per group i, on three streams:
+// independent convolution).  Group boundaries fall on image counts whose
+// output offset is a multiple of 16 bytes (the kernels' alignment rule): with
+// out_h*out_w*K odd, every fourth image; input offsets are always aligned
+// (C % 16 == 0).  Per group i, on three streams:
 //   h2d stream:  copy input images of group i          -> event in[i]
 //   compute:     wait in[i]; launch on group i's shape  -> event done[i]
 //   d2h stream:  wait done[i]; copy output rows of group i
@@ -64,12 +67,16 @@ int8conv_status launch_host_pipeline(int strategy, const int8conv_shape &s, cons
   PipelineState &p = g_pipes[dev.device & 63];
   std::lock_guard<std::mutex> lock(p.mutex);
   if (!init_pipe(p)) return INT8CONV_CUDA_ERROR;
-  if (chunks < 1) chunks = 1;
-  if (chunks > s.n) chunks = s.n;
-  if (chunks > kMaxChunks) chunks = kMaxChunks;
   const int32_t out_h = i8c_out_h(&s), out_w = i8c_out_w(&s);
   const size_t in_image = static_cast<size_t>(s.h) * s.w * s.c;
   const size_t out_image = static_cast<size_t>(out_h) * out_w * s.k;
+  // Images per boundary unit: the output offset of `step` images is a
+  // multiple of four int32 values.
+  const int step = out_image % 4 == 0 ? 1 : out_image % 2 == 0 ? 2 : 4;
+  const int units = (s.n + step - 1) / step;
+  if (chunks < 1) chunks = 1;
+  if (chunks > units) chunks = units;
+  if (chunks > kMaxChunks) chunks = kMaxChunks;
   auto ok = [](cudaError_t e) { return e == cudaSuccess; };
   // On an error part-way through, copies already queued may still be reading
   // or writing the caller's host buffers: wait for them before returning, so
@@ -89,7 +96,8 @@ int8conv_status launch_host_pipeline(int strategy, const int8conv_shape &s, cons
     return fail(INT8CONV_CUDA_ERROR);
   int first = 0;
   for (int c = 0; c < chunks; ++c) {
-    const int last = static_cast<int>((static_cast<int64_t>(s.n) * (c + 1)) / chunks);
+    const int64_t unit_end = static_cast<int64_t>(units) * (c + 1) / chunks;
+    const int last = unit_end * step < s.n ? static_cast<int>(unit_end * step) : s.n;
     const int images = last - first;
     int8conv_shape part = s;
     part.n = images;

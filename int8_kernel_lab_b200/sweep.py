@@ -53,21 +53,26 @@ def _ms(value: str) -> float:
         return -1.0
 
 
-def merge_repeats(rows: list) -> dict:
+def merge_repeats(rows: list, expected: int = 0) -> dict:
     """One row from several conv_lab rows of the same case: mean launch times
     (-1 unless every repetition timed the family), correctness only if every
-    repetition validated, winner / tops / roofline_frac from the means."""
+    repetition validated and all `expected` repetitions returned a row,
+    winner / tops / roofline_frac from the means.  graph_ms is the winner's
+    graph time in each row, so it is averaged over the repetitions whose
+    winner is the merged winner only (-1 if none)."""
     merged = dict(rows[0])
-    for column in [f + "_ms" for f in FAMILIES] + ["graph_ms"]:
+    for column in [f + "_ms" for f in FAMILIES]:
         if column not in merged:
             continue
         values = [_ms(r.get(column)) for r in rows]
         merged[column] = ("%.6g" % (sum(values) / len(values))
                           if all(v >= 0 for v in values) else "-1")
+    complete = len(rows) >= expected
     for f in FAMILIES:
         column = f + "_correct"
         if column in merged:
-            merged[column] = "1" if all(r.get(column) == "1" for r in rows) else "0"
+            merged[column] = ("1" if complete and all(r.get(column) == "1" for r in rows)
+                              else "0")
     timed = {f: _ms(merged[f + "_ms"]) for f in FAMILIES if f + "_ms" in merged}
     timed = {f: v for f, v in timed.items() if v >= 0}
     if "winner" in merged:
@@ -80,6 +85,10 @@ def merge_repeats(rows: list) -> dict:
             for column in ("tops", "roofline_frac"):
                 if _ms(merged.get(column)) >= 0:
                     merged[column] = "%.6g" % (_ms(merged[column]) * scale)
+    if "graph_ms" in merged:
+        same = [_ms(r.get("graph_ms")) for r in rows if r.get("winner") == merged.get("winner")]
+        same = [v for v in same if v >= 0]
+        merged["graph_ms"] = "%.6g" % (sum(same) / len(same)) if same else "-1"
     merged["repeats"] = str(len(rows))
     return merged
 
@@ -102,6 +111,8 @@ def main(argv=None) -> int:
     ap.add_argument("--cudnn-root", default="")
     ap.add_argument("--repeat", type=int, default=1,
                     help="run the case list this many times, interleaved, and write means")
+    ap.add_argument("--rotate-l2", action="store_true",
+                    help="time every launch on rotating buffer sets (L2-cold)")
     args = ap.parse_args(argv)
     if args.repeat < 1:
         raise SystemExit("--repeat must be at least 1")
@@ -115,10 +126,12 @@ def main(argv=None) -> int:
         raise SystemExit(f"unknown cases: {', '.join(unknown)}")
     args.output.parent.mkdir(parents=True, exist_ok=True)
     runs = {}  # case -> list of conv_lab rows, one per repetition
+    attempts = {}  # case -> repetitions run so far (a failed run returns no row)
     status = 0
     shapes = {r["name"]: r for r in rows}
     for rep in range(args.repeat):
         for case in requested:
+            attempts[case] = attempts.get(case, 0) + 1
             r = shapes[case]
             oh = int((int(r["h"]) + 2 * int(r["pad_h"]) -
                       int(r["dilation_h"]) * (int(r["r"]) - 1) - 1) / int(r["stride_h"])) + 1
@@ -127,6 +140,8 @@ def main(argv=None) -> int:
             ops = (2.0 * int(r["n"]) * oh * ow * int(r["k"]) * int(r["c"]) * int(r["r"]) *
                    int(r["s"]))
             extra = ["--validate-samples", "200000"] if ops > args.full_validate_ops else []
+            if args.rotate_l2:
+                extra.append("--rotate-l2")
             result = subprocess.run(
                 [args.conv_lab, "--case", case, "--config", str(args.configs), "--strategy",
                  args.strategy, "--iterations", str(args.iterations), "--warmup",
@@ -145,7 +160,8 @@ def main(argv=None) -> int:
             for name in requested:
                 if name not in runs:
                     continue
-                m = merge_repeats(runs[name]) if args.repeat > 1 else dict(runs[name][0])
+                m = (merge_repeats(runs[name], attempts[name]) if args.repeat > 1
+                     else dict(runs[name][0]))
                 if args.with_cudnn:
                     m.update(dispatch_ms=dispatch_ms(m), cudnn_ms="", cudnn_over_dispatch="",
                              comparison_contract="cudnn_not_built")

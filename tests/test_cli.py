@@ -14,7 +14,7 @@ REFERENCE_COLUMNS = ["case", "n", "h", "w", "c", "k", "r", "s", "out_h", "out_w"
                      "generic_ms", "strip_ms", "winner", "generic_correct", "strip_correct"]
 APPENDED = ["eligible_halo", "eligible_splitk", "halo_ms", "splitk_ms", "halo_correct",
             "splitk_correct", "gpus", "tops", "roofline_frac", "oracle_ms", "oracle_threads",
-            "graph_ms", "selected", "epilogue"]
+            "graph_ms", "selected", "epilogue", "l2"]
 
 
 def run(*args):
@@ -72,20 +72,3 @@ def test_int8_epilogues_validate(case, epilogue):
     row = next(csv.DictReader(io.StringIO(out.stdout)))
     assert row["epilogue"] == epilogue
     assert all(row[f + "_correct"] == "1" for f in ("generic", "strip", "halo", "splitk"))
-
-
-PEAK = ROOT / "int8_kernel_lab_b200" / "lib" / "mma_peak"
-
-
-def test_mma_peak_rejects_bad_options():
-    for args in (["--bogus"], ["--ms", "0"], ["--launches", "0"]):
-        out = subprocess.run([str(PEAK), *args], capture_output=True, text=True, timeout=60)
-        assert out.returncode == 2 and "mma_peak" in out.stderr
-
-
-@pytest.mark.gpu
-def test_mma_peak_runs():
-    out = subprocess.run([str(PEAK), "--ms", "20", "--launches", "2"], capture_output=True,
-                         text=True, timeout=120)
-    assert out.returncode == 0, out.stderr
-    assert '"metric": "int8_tensor_tops"' in out.stdout.splitlines()[-1]

@@ -321,6 +321,29 @@ def test_host_buffer_pipeline(cuda, chunks):
     assert np.array_equal(hy.numpy(), pyoracle.conv(shape, x, w, b))
 
 
+@pytest.mark.parametrize("chunks", [2, 3, 5])
+def test_host_buffer_pipeline_unaligned_image_outputs(cuda, chunks):
+    # out_h*out_w*K odd (7 x 7 output, K = 63): an image's output is not a
+    # whole number of 16-byte groups, so group boundaries must fall on every
+    # fourth image for the kernels' 16-byte alignment rule.
+    torch = cuda
+    shape = m.ConvShape(9, 7, 7, 32, 63, 3, 3, 1, 1, 1, 1, 1, 1)
+    x, w, b = m.make_inputs(shape, seed=chunks)
+    hx, hw, hb = (torch.from_numpy(a).pin_memory() for a in (x, w, b))
+    hy = torch.full((shape.output_elements,), -1, dtype=torch.int32).pin_memory()
+    dx = torch.empty(shape.input_elements, dtype=torch.int8, device="cuda")
+    dw = torch.empty(shape.filter_elements, dtype=torch.int8, device="cuda")
+    db = torch.empty(shape.k, dtype=torch.int32, device="cuda")
+    dy = torch.empty(shape.output_elements, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    for strategy in ("auto", "generic", "splitk"):
+        hy.fill_(-1)
+        m.launch_host(strategy, shape, hx, hw, hb, hy, dx, dw, db, dy, chunks=chunks, stream=s)
+        s.synchronize()
+        assert m.device_status() == _abi.OK
+        assert np.array_equal(hy.numpy(), pyoracle.conv(shape, x, w, b)), strategy
+
+
 def test_output_beyond_2g_elements(cuda):
     # Maximum-size indexing: 2^21 output rows x 1040 channels = 2.18e9 int32
     # outputs (8.7 GB), past 2^31 elements, with five 208-wide N tiles.  The

@@ -140,4 +140,18 @@ def test_repeat_means_and_correctness(tmp_path):
     # (generic, 0.018 mean) gives the same time, so the same TOPS.
     assert float(m["tops"]) == pytest.approx(10.0)
     assert float(m["roofline_frac"]) == pytest.approx(0.5)
-    assert float(m["graph_ms"]) == pytest.approx(0.005)
+    # graph_ms is each row's winner's graph time: only the repetition whose
+    # winner is the merged winner (b, generic) counts.
+    assert float(m["graph_ms"]) == pytest.approx(0.004)
+
+
+def test_repeat_with_a_missing_row_is_not_correct():
+    # Three repetitions ran, two returned a row: no family counts as correct.
+    a = {"case": "x", "generic_ms": "0.020", "strip_ms": "-1", "halo_ms": "-1",
+         "splitk_ms": "-1", "winner": "generic", "generic_correct": "1", "strip_correct": "1",
+         "halo_correct": "1", "splitk_correct": "1", "tops": "10", "roofline_frac": "0.5",
+         "graph_ms": "0.006"}
+    m = sweep.merge_repeats([a, dict(a)], expected=3)
+    assert m["generic_correct"] == "0" and m["repeats"] == "2"
+    assert sweep.merge_repeats([a, dict(a)], expected=2)["generic_correct"] == "1"
+    assert float(sweep.merge_repeats([a, dict(a)])["graph_ms"]) == pytest.approx(0.006)
