@@ -1142,12 +1142,12 @@ static int8conv_status launch_cblk(const int8conv_shape &s, const ConvGeom &g, i
 }
 
 // CTA pairs halve the filter bytes per output row.  Measured on B200 they pay
-// off when the filter tile is the full 256 columns, there is at least one wave
+// off when the filter tile is at least 192 columns, there is at least one wave
 // of 256-row tiles, and either the reduction is deep (R*S*C >= 1024: 5a 354 vs
-// 401 us, 5b 92 vs 102 us) or there are many waves (big_1x1_s1, 4096 tiles:
-// 262 vs 266 us).  Narrower, shallower or smaller layers run faster as single
-// CTAs (3b: 17 vs 23 us, nonmultiple8_k255: 61 vs 65 us, batch16 bottleneck
-// expand: 24 vs 27 us).
+// 401 us, 5b 92 vs 102 us, 5c with 192 columns 35.2 vs 36.6 us) or there are
+// many waves (big_1x1_s1, 4096 tiles: 262 vs 266 us).  Narrower, shallower or
+// smaller layers run faster as single CTAs (3b: 17 vs 23 us,
+// nonmultiple8_k255: 61 vs 65 us, batch16 bottleneck expand: 24 vs 27 us).
 static bool use_pair(const int8conv_shape &s, int mode, int out_kind) {
   const int pairing = pairing_mode();
   if (pairing == 1 || mode == kModeGather) return false;  // the gather warp feeds one CTA
@@ -1156,7 +1156,7 @@ static bool use_pair(const int8conv_shape &s, int mode, int out_kind) {
   if (!plan_geometry(s, mode, true, out_kind, device_info().sm_count / 2, g, cblk)) return false;
   if (pairing == 2) return true;
   const int64_t reduction = static_cast<int64_t>(s.r) * s.s * s.c;
-  return g.bn == 256 && g.num_tiles >= device_info().sm_count &&
+  return g.bn >= 192 && g.num_tiles >= device_info().sm_count &&
          (reduction >= 1024 || g.num_tiles >= 1024);
 }
 

@@ -14,6 +14,8 @@
 //     halo_correct, splitk_correct, gpus, tops, roofline_frac, oracle_ms,
 //     oracle_threads, graph_ms, selected (the family int8conv_select picks),
 //     epilogue, l2 ("warm", or "rotated:<sets>" with --rotate-l2).
+// --staging gather runs GENERIC with its gather warp on every shape
+// (int8conv_set_generic_staging), to time it against the im2col staging.
 // --rotate-l2 times every launch on the next of enough input/output sets
 // that together span twice the L2, so memory-bound shapes are timed L2-cold
 // (the reference times one buffer set, L2-warm for small shapes).
@@ -91,6 +93,7 @@ struct Options {
   long long validate_samples = 0;  // 0: every output
   std::string epilogue = "int32";  // int32 | int8 (NHWC) | int8x32 (NCHW_VECT_C)
   bool rotate_l2 = false;          // time over rotating buffer sets (L2-cold)
+  int staging = 0;                 // GENERIC staging: 0 auto, 1 gather
 };
 
 [[noreturn]] void usage() {
@@ -98,7 +101,7 @@ struct Options {
                "[--warmup N] [--iterations N] [--case NAME] [--config CSV] "
                "[--values full|reference] [--seed S] [--batch N] [--peak-tops T] "
                "[--no-graph] [--pairing auto|single|pair] [--validate-samples N] "
-               "[--epilogue int32|int8|int8x32] [--rotate-l2]\n";
+               "[--epilogue int32|int8|int8x32] [--rotate-l2] [--staging auto|gather]\n";
   std::exit(EXIT_FAILURE);
 }
 
@@ -113,6 +116,11 @@ Options parse_options(int argc, char **argv) {
     if (arg == "--csv") o.csv = true;
     else if (arg == "--no-graph") o.graph = false;
     else if (arg == "--rotate-l2") o.rotate_l2 = true;
+    else if (arg == "--staging") {
+      const std::string v = value();
+      o.staging = v == "auto" ? 0 : v == "gather" ? 1 : -1;
+      if (o.staging < 0) usage();
+    }
     else if (arg == "--strategy") o.strategy = value();
     else if (arg == "--warmup") o.warmup = std::stoi(value());
     else if (arg == "--iterations") o.iterations = std::stoi(value());
@@ -334,6 +342,7 @@ int run_lab(int argc, char **argv) {
   }
   const Options options = parsed;
   int8conv_set_cta_pairing(options.pairing);
+  int8conv_set_generic_staging(options.staging);
   const std::string config = options.config.empty() ? default_config(argv[0]) : options.config;
   int8conv_shape shape;
   if (!load_case(config, options.case_name, shape)) {

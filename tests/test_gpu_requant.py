@@ -150,3 +150,31 @@ def test_requant_edge_values_on_device(cuda, layout):
                 got = _run(cuda, fam, shape, x, w, b, mult, expo, zp, relu, layout)
                 bad = np.flatnonzero(got != want)
                 assert bad.size == 0, (fam, trial, zp, relu, bad[:5], got[bad[:5]], want[bad[:5]])
+
+
+def test_device_meets_hand_derived_known_answers(cuda):
+    # The published rule's known answers (derived by hand, not by the oracle):
+    # INT32_MIN * INT32_MIN, saturating left shifts, ties at every exponent of
+    # the rounding divide.  A zero filter makes t = bias[k]; each channel
+    # carries one (t, multiplier, exponent) row, and rows sharing a zero
+    # point and ReLU flag run in one launch.
+    from test_requant_cpu import Q30, TIES, known_answer_table
+
+    rows = known_answer_table() + [
+        (sign * (2 * k + 1) * 2 ** n, Q30, -n, 0, 0, sign * (k + 1)) for n, k, sign in TIES]
+    groups = {}
+    for row in rows:
+        groups.setdefault((row[3], row[4]), []).append(row)
+    for (zp, relu), group in groups.items():
+        k = len(group)
+        shape = m.ConvShape(1, 2, 3, 16, k, 1, 1, 0, 0, 1, 1, 1, 1)
+        x = np.zeros(shape.input_elements, np.int8)
+        w = np.ones(shape.filter_elements, np.int8)
+        b = np.array([r[0] for r in group], np.int64).astype(np.int32)
+        mult = np.array([r[1] for r in group], np.int64).astype(np.int32)
+        expo = np.array([r[2] for r in group], np.int32)
+        want = np.tile(np.array([r[5] for r in group], np.int8), shape.out_h * shape.out_w)
+        for fam in ("generic", "auto"):
+            got = _run(cuda, fam, shape, x, w, b, mult, expo, zp, bool(relu), "nhwc")
+            bad = np.flatnonzero(got != want)
+            assert bad.size == 0, (fam, zp, relu, [group[i % k] for i in bad[:4]], got[bad[:4]])

@@ -122,3 +122,50 @@ def test_vect_c_needs_k_multiple_of_32():
     shape = m.load_workloads()["cfg4c_tail_k100"]
     rq = _abi.CRequant(1 << 20, 1 << 20, 0, 0, _abi.LAYOUT_NCHW_VECT_C)
     assert _abi.lib.int8conv_launch_requant(*_launch_args(shape, rq)) == _abi.NOT_ELIGIBLE
+
+
+# Ties at every exponent of the rounding divide.  With the multiplier 2^30 the
+# doubling high multiply halves an even t exactly, so u = t / 2; the divide by
+# 2^n then sees u = +-(2k+1) * 2^(n-1), exactly half way, and the published
+# rule (gemmlowp RoundingDivideByPOT) rounds it away from zero to +-(k+1).
+TIES = [(n, k, sign) for n in range(1, 31) for k in (0, 1, 2) for sign in (1, -1)
+        if (2 * k + 1) * 2 ** n <= I32_MAX]
+
+
+@pytest.mark.parametrize("n, k, sign", TIES)
+def test_requant_ties_round_away_from_zero_at_every_exponent(n, k, sign):
+    t = sign * (2 * k + 1) * 2 ** n
+    want = sign * (k + 1)
+    assert pyoracle.requant_value(t, Q30, -n, 0, 0) == want
+    assert pyoracle.requant_value_py(t, Q30, -n, 0, 0) == want
+    # one below the tie in magnitude rounds toward zero instead
+    assert pyoracle.requant_value(t - sign * 2, Q30, -n, 0, 0) == sign * k
+
+
+def known_answer_table():
+    """(t, multiplier, exponent, zero_point, relu, want) rows derived by hand
+    from the rule in include/int8conv.h; shared with the GPU test."""
+    rows = [
+        # doubling high multiply of INT32_MIN by itself saturates to INT32_MAX,
+        # then / 2^31 rounds (2^31 - 1) / 2^31 up to 1
+        (I32_MIN, I32_MIN, 0, 0, 0, 127), (I32_MIN, I32_MIN, -31, 0, 0, 1),
+        (I32_MIN, I32_MIN, -31, -7, 0, -6),
+        # saturating left shift: -3e8 * 8 is below INT32_MIN and saturates there
+        # (a wrapping shift would give +1.89e9 and 127); * 0.5 -> -2^30 -> -128
+        (-300000000, Q30, 3, 0, 0, -128), (300000000, Q30, 3, 0, 0, 127),
+        # the left shift alone, inside int32: 40 * 2^2 * 0.5 = 80
+        (40, Q30, 2, 0, 0, 80), (-40, Q30, 2, 0, 0, -80),
+        # negative ties at exponent -1 .. -3 through a full multiplier
+        (-6, Q30, -1, 0, 0, -2), (-12, Q30, -2, 0, 0, -2), (-24, Q30, -3, 0, 0, -2),
+        (6, Q30, -1, 0, 0, 2), (12, Q30, -2, 0, 0, 2), (24, Q30, -3, 0, 0, 2),
+        # ReLU clamps at the zero point, after the zero point is added
+        (-6, Q30, -1, 5, 1, 5), (60, Q30, -1, 5, 1, 20),
+    ]
+    return rows
+
+
+@pytest.mark.parametrize("row", known_answer_table())
+def test_requant_published_rule_known_answers(row):
+    t, mult, e, zp, relu, want = row
+    assert pyoracle.requant_value(t, mult, e, zp, relu) == want
+    assert pyoracle.requant_value_py(t, mult, e, zp, relu) == want
