@@ -629,7 +629,7 @@ def verify_sharded(full, x, w, b, y_timed, y_e2e, dist, rank, world, clocks):
 
     from int8_kernel_lab_b200.sharding import gather_outputs, shard_range
     gathered = gather_outputs(y_timed, full, rank, world, dist)
-    gathered_e2e = gather_outputs(y_e2e.cuda(), full, rank, world, dist)
+    gathered_e2e = gather_outputs(y_e2e.to(y_timed.device), full, rank, world, dist)
     records = [None] * world
     dist.all_gather_object(records, clocks)
     if rank != 0:
