@@ -7,7 +7,8 @@
 //   out[m*K + k] = bias[k] + sum_{r,s,c} X[n, oy*sh + r*dh - ph, ox*sw + s*dw - pw, c] * W[k,r,s,c]
 // with padding taps contributing nothing (here: zero-filled by TMA).
 //
-// B200 design (persistent CTAs, 6 warps each; 18 with the int8 epilogue):
+// B200 design (persistent CTAs, 6 warps each; 18 with the int8 epilogue;
+// 3 more with the gather staging):
 //   warp 0     TMA producer.  Activations come through an im2col tensor map
 //              (padding, stride and dilation are done by the TMA unit:
 //              bounding-box corners, traversal strides, per-tap offsets),
@@ -54,8 +55,9 @@
 //   (S-1)*dw positions per channel block feeds all R*S taps, tap (r, s)
 //   reading it r*dh*Wp + s*dw rows further on.
 // GATHER (GENERIC on shapes the im2col tensor map cannot encode: stride > 8,
-//   pad > 127, tap span > 127): warp 0's 32 lanes stage the same 128-row
-//   tiles with asynchronous 16-byte copies into the same swizzled layout
+//   pad > 127, tap span > 127): four gather warps (warp 0 and three after
+//   the epilogue's) stage the same 128-row tiles, 32 rows each, with
+//   asynchronous 16-byte copies into the same swizzled layout
 //   (gather_producer); the filter, the MMA issuer and the epilogue are
 //   GENERIC's.  Single CTAs only.
 // The reference's odd-K epilogue bug (generic_implicit_gemm.cuh:218-225) has
@@ -87,7 +89,8 @@ struct SwizzleOf<32> {
   static constexpr Layout kLayout = Layout::kSw32;
 };
 
-// Epilogue staging: 4 warps x 2 buffers x (32 rows x 128 B).
+// Epilogue staging: 4 warps x 2 buffers x (32 rows x 128 B) (int32 output),
+// or 16 warps x (32 x 32 B block + channel tables) (int8 output).
 constexpr uint32_t kEpilogueStaging = 4 * 2 * 32 * 128;
 constexpr uint32_t kOneCtaPerSm = kMaxSmem / 2 + 1024;
 
@@ -177,21 +180,27 @@ __device__ __forceinline__ void commit_to(uint64_t *bar) {
     umma_commit(bar);
 }
 
-// GATHER producer (warp 0, all 32 lanes): GENERIC's A tiles for shapes the
-// im2col tensor map cannot encode (stride > 8, pad > 127, tap span > 127, or a
-// bounding-box corner out of range), in the same swizzled layout TMA would
-// write, so the MMA issuer and the epilogue are GENERIC's.  This is the
-// reference's gather (generic_implicit_gemm.cuh:46-69: 16-byte vectors at
-// (n, iy, ix, c), zero for padding taps and rows past M) done with
-// asynchronous 16-byte copies that keep `g.gather_lag` k-blocks in flight.
+// GATHER producer: GENERIC's A tiles for shapes the im2col tensor map cannot
+// encode (stride > 8, pad > 127, tap span > 127, or a bounding-box corner out
+// of range), in the same swizzled layout TMA would write, so the MMA issuer
+// and the epilogue are GENERIC's.  This is the reference's gather
+// (generic_implicit_gemm.cuh:46-69: 16-byte vectors at (n, iy, ix, c), zero
+// for padding taps and rows past M) done by kGatherWarps warps with
+// asynchronous 16-byte copies, each warp owning 32 rows of the 128-row tile
+// and keeping `g.gather_lag` k-blocks in flight.
 //
-// Per tile the warp tabulates each row's image offset and input origin
-// (img*H, oy*sh - ph, ox*sw - pw) in shared memory; per k-block (tap r,s x
-// channel block) lane (row sub-index, 16-byte chunk) copies its chunk of
-// every (32 / chunks)-th row.  A k-block is published once every lane's
-// copies have landed: each lane fences its generic-proxy writes for the
-// tensor cores' async-proxy reads and arrives on the stage's barrier, which
-// also counts the filter tile's TMA bytes (lane 0 arms and issues it).
+// Per tile a warp tabulates, in shared memory, each of its rows' input
+// origin (oy*sh - ph, ox*sw - pw) and that origin's byte offset in X; per
+// k-block (tap r,s x channel block) the tap's offset (r*dh*W + s*dw)*C is the
+// same for every row, so a 16-byte chunk costs a bounds check and an add.
+// Lane (row sub-index, 16-byte chunk) copies its chunk of every
+// (32 / chunks)-th row of the warp's 32.  A k-block is published once every
+// lane's copies have landed: each lane fences its generic-proxy writes for
+// the tensor cores' async-proxy reads and arrives on the stage's barrier,
+// which also counts the filter tile's TMA bytes (warp 0's lane 0 arms and
+// issues it): 1 + 32 * kGatherWarps arrivals per phase.
+constexpr int kGatherWarps = 4;
+
 template <int CBLK>
 __device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t *__restrict__ x,
                                                 const CUtensorMap *tmap_w, uint8_t *a_ring,
@@ -199,18 +208,21 @@ __device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t 
                                                 int4 *rowtab, uint64_t *b_full,
                                                 uint64_t *b_empty, const RunCtl &ctl,
                                                 const WaitCtx &wctx, int tile_first,
-                                                int tile_step, int lane) {
+                                                int tile_step, int gw, int lane) {
   constexpr int kChunks = CBLK / 16;          // 16-byte chunks per row
   constexpr int kRowsPerPass = 32 / kChunks;  // rows one warp-wide pass covers
-  constexpr int kPasses = kBlockM / kRowsPerPass;
+  constexpr int kPasses = 32 / kRowsPerPass;  // passes over the warp's 32 rows
   constexpr uint32_t kSwMask = kChunks - 1;   // 128/64/32-byte swizzle: chunk ^= row bits
   const int chunk = lane % kChunks;
   const int rsub = lane / kChunks;
+  const int row_base = 32 * gw;               // this warp's rows of the tile
   const int lag = g.gather_lag;
+  const bool loads_filter = gw == 0 && lane == 0;
+  int4 *mytab = rowtab + row_base;
   Ring rb;           // next stage to fill
   Ring rp;           // oldest stage filled but not yet published
   int pending = 0;   // k-blocks issued and not yet published
-  long armed_b = 0;  // filter loads issued (lane 0)
+  long armed_b = 0;  // filter loads issued (warp 0, lane 0)
   auto publish = [&]() {
     // This lane's copies of the k-block are complete (cp_async_wait);
     // make them visible to the async proxy, then arrive.
@@ -222,21 +234,25 @@ __device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t 
   bool ok = true;
   for (int tile = tile_first; tile < g.num_units && ok; tile += tile_step) {
     const Unit t = unit_at(g, tile);
-    const int m0 = t.m_tile * kBlockM;
-    // Row table of this tile (every lane has issued the previous tile's
-    // copies, whose source addresses are already in registers).
+    // Row table of this warp's 32 rows (every lane has issued the previous
+    // tile's copies, whose source addresses are already in registers):
+    // input origin and its byte offset.  Rows past M get an origin no tap
+    // can bring inside the image.
     __syncwarp();
-    for (int i = lane; i < kBlockM; i += 32) {
-      const int m = m0 + i;
-      int4 e = make_int4(0, -(1 << 30), -(1 << 30), 0);  // rows past M: every tap is padding
+    {
+      const int m = t.m_tile * kBlockM + row_base + lane;
+      int4 e = make_int4(-(1 << 30), -(1 << 30), 0, 0);
       if (m < g.M) {
         const int img = m / g.PQ;
         const int rem = m - img * g.PQ;
         const int oy = rem / g.Q;
         const int ox = rem - oy * g.Q;
-        e = make_int4(img * g.H, oy * g.stride_h - g.pad_h, ox * g.stride_w - g.pad_w, 0);
+        const int iy0 = oy * g.stride_h - g.pad_h;
+        const int ix0 = ox * g.stride_w - g.pad_w;
+        const int64_t off = ((static_cast<int64_t>(img) * g.H + iy0) * g.W + ix0) * g.C;
+        e = make_int4(iy0, ix0, static_cast<int>(off & 0xffffffffll), static_cast<int>(off >> 32));
       }
-      rowtab[i] = e;
+      mytab[lane] = e;
     }
     __syncwarp();
     int cb = 0, r = 0, s = 0, tap = 0;
@@ -247,7 +263,7 @@ __device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t 
         break;
       }
       if (!ctl.starve) {
-        if (lane == 0) {
+        if (loads_filter) {
           mbar_arrive_expect_tx(&b_full[rb.stage], plan.b_bytes);
           tma_load_3d(b_ring + rb.stage * plan.b_bytes, tmap_w, &b_full[rb.stage], cb * CBLK, tap,
                       t.n0);
@@ -258,18 +274,18 @@ __device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t 
         const int dx = s * g.dil_w;
         const int c_off = cb * CBLK + chunk * 16;
         const bool c_ok = c_off < g.C;
-#pragma unroll 8
+        const int64_t tap_off = (static_cast<int64_t>(dy) * g.W + dx) * g.C + c_off;
+#pragma unroll
         for (int i = 0; i < kPasses; ++i) {
-          const int row = rsub + i * kRowsPerPass;
+          const int row = row_base + rsub + i * kRowsPerPass;
           const int4 e = rowtab[row];
-          const int iy = e.y + dy;
-          const int ix = e.z + dx;
-          const bool in = c_ok && static_cast<unsigned>(iy) < static_cast<unsigned>(g.H) &&
-                          static_cast<unsigned>(ix) < static_cast<unsigned>(g.W);
-          const int8_t *src =
-              in ? x + (static_cast<int64_t>(e.x + iy) * g.W + ix) * g.C + c_off : x;
-          const uint32_t off = static_cast<uint32_t>(row * CBLK + chunk * 16);
-          cp_async_16(a_base + (off ^ (((off >> 7) & kSwMask) << 4)), src, in ? 16u : 0u);
+          const bool in = c_ok && static_cast<unsigned>(e.x + dy) < static_cast<unsigned>(g.H) &&
+                          static_cast<unsigned>(e.y + dx) < static_cast<unsigned>(g.W);
+          const int64_t off =
+              (static_cast<int64_t>(e.w) << 32 | static_cast<uint32_t>(e.z)) + tap_off;
+          const int8_t *src = in ? x + off : x;
+          const uint32_t so = static_cast<uint32_t>(row * CBLK + chunk * 16);
+          cp_async_16(a_base + (so ^ (((so >> 7) & kSwMask) << 4)), src, in ? 16u : 0u);
         }
         cp_async_commit();
         ++pending;
@@ -299,7 +315,7 @@ __device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t 
   cp_async_wait<0>();
   while (pending > 0) publish();
   // The filter loads armed most recently land before the CTA exits.
-  if (lane == 0) {
+  if (loads_filter) {
     for (long i = 0, n = armed_b < g.stages ? armed_b : g.stages; i < n; ++i) {
       rb.prev(g.stages);
       mbar_wait(&b_full[rb.stage], rb.phase, wctx, kStatusTimeoutTeardown);
@@ -341,18 +357,22 @@ __device__ __forceinline__ void requant_block(const uint32_t (&v)[32], const int
 // Epilogue warps: 4 for int32 output (one per TMEM lane quarter); 16 for the
 // requantised int8 output, whose per-element fixed-point arithmetic needs the
 // issue slots (four warps per lane quarter, each owning every fourth
-// 32-column block).
+// 32-column block).  Eight int32 warps (two per quarter, one staging buffer
+// each) were measured on B200 and dropped: 5a and 5c unchanged within 2 %,
+// 3b 15.8 -> 17.7 us and the launch-bound shapes 0.4-0.7 us slower.
 template <bool REQ>
 constexpr int epilogue_warps() {
   return REQ ? 16 : 4;
 }
-template <bool REQ>
+// Threads of a launch: producer and MMA warps, the epilogue warps, and for
+// the gather staging its three more gather warps (after the epilogue's).
+template <int MODE, bool REQ>
 constexpr int kernel_threads() {
-  return 64 + 32 * epilogue_warps<REQ>();
+  return 64 + 32 * epilogue_warps<REQ>() + (MODE == kModeGather ? 32 * (kGatherWarps - 1) : 0);
 }
 
 template <int CBLK, int MODE, bool PAIR, bool REQ>
-__global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
+__global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
     conv_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_w,
                 const __grid_constant__ CUtensorMap tmap_y, const ConvGeom g,
@@ -402,7 +422,7 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
     }
     for (int i = 0; i < g.stages; ++i) {
       // GATHER: the filter load's arrival plus one per gather lane.
-      mbar_init(&b_full[i], GATHER ? 33 : 1);
+      mbar_init(&b_full[i], GATHER ? 1 + 32 * kGatherWarps : 1);
       mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -436,10 +456,12 @@ __global__ void __launch_bounds__(kernel_threads<REQ>(), 1)
   griddep_wait();
   griddep_launch_dependents();
 
-  if (warp == 0 && GATHER) {
+  constexpr int kFirstExtraGather = 2 + epilogue_warps<REQ>();
+  if (GATHER && (warp == 0 || warp >= kFirstExtraGather)) {
     gather_producer<CBLK>(g, x, &tmap_w, a_ring, b_ring, plan,
                           reinterpret_cast<int4 *>(smem + plan.rows_off), b_full, b_empty, ctl,
-                          wctx, tile_first, tile_step, lane);
+                          wctx, tile_first, tile_step,
+                          warp == 0 ? 0 : warp - kFirstExtraGather + 1, lane);
   } else if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
@@ -1120,7 +1142,7 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   LaunchPlan lp;
   lp.func = reinterpret_cast<const void *>(kernel);
   lp.grid = dim3(ctas, 1, 1);
-  lp.block = dim3(kernel_threads<REQ>(), 1, 1);
+  lp.block = dim3(kernel_threads<MODE, REQ>(), 1, 1);
   lp.smem = smem_bytes;
   lp.cluster = PAIR ? 2 : 1;
   plan_args(lp, maps[0], maps[1], maps[2], g, x, b, static_cast<int32_t *>(y), RunCtl{}, rq);
