@@ -159,7 +159,11 @@ int int8conv_select(const int8conv_shape *shape) {
   //    STRIP's strip reuse no longer pays once the epilogue uses TMA stores
   //    (5a 357 vs 396 us, 5c 39 vs 51 us).
   //  * SPLITK when the layer has too few 128-row output tiles to occupy half
-  //    the GPU but a reduction deep enough to split (7x7 and 14x14 layers).
+  //    the GPU but a reduction deep enough to split (7x7 and 14x14 layers):
+  //    at least 10 k-blocks.  With 8 or 9 (a 1x1 over C = 1024, a 3x3 over
+  //    C <= 128) GENERIC's tail-balanced column parts are as fast or faster
+  //    (51-workload sweep on one B200: darknet_res_13_reduce 13.6 vs 15.0 us,
+  //    dilated_3x3 13.6 vs 15.0, cfg1_smoke 13.5 vs 13.7).
   //    The split must fit in one wave of resident clusters (B200 table):
   //    two waves lost to GENERIC in the sweep (batch8_3x3, darknet_down_52).
   //  * Except where GENERIC runs narrow N tiles (i8c_generic_bn): those fill
@@ -181,7 +185,7 @@ int int8conv_select(const int8conv_shape *shape) {
   const int32_t cblk = i8c_channel_block(shape->c);
   const int64_t kblocks =
       static_cast<int64_t>(shape->r) * shape->s * ((shape->c + cblk - 1) / cblk);
-  if (int8conv_eligible(shape, INT8CONV_SPLITK) && tiles < 74 && kblocks >= 8 &&
+  if (int8conv_eligible(shape, INT8CONV_SPLITK) && tiles < 74 && kblocks >= 10 &&
       i8c_split_count(i8c_split_tiles(shape), kblocks, clusters) >= 2)
     return INT8CONV_SPLITK;
   return INT8CONV_GENERIC;

@@ -86,11 +86,25 @@ def test_narrow_generic_tiles_take_the_small_odd_k_layer():
     # the 51 workloads only 4c (K = 100, bn 112 -> four 32-column tiles)
     # qualifies, and there GENERIC beat SPLITK on B200 (13.4-13.8 against
     # 15.1-15.2 us per launch).
+    # smoke (K = 32, nine k-blocks) takes GENERIC by the k-block threshold
+    # of split-K instead (test_splitk_needs_ten_kblocks).
     table = m.load_workloads()
     picked = {name for name, s in table.items()
               if s.select() == "generic" and s.eligible("splitk") and s.k % 64 != 0
               and (s.n * s.out_h * s.out_w + 127) // 128 < 148}
-    assert picked == {"cfg4c_tail_k100"}
+    assert picked == {"cfg4c_tail_k100", "smoke"}
+
+
+def test_splitk_needs_ten_kblocks():
+    # Split-K only with at least ten k-blocks (tap x channel block): with 8 or
+    # 9, GENERIC's tail-balanced column parts were as fast or faster on B200
+    # (darknet_res_13_reduce 13.6 vs 15.0 us, dilated_3x3 13.6 vs 15.0).
+    table = m.load_workloads()
+    for name in ("darknet_res_13_reduce", "darknet_detect_13_padded", "dilated_3x3",
+                 "cfg1_smoke", "resnet_s3_3x3"):
+        assert table[name].select() == "generic", name
+    for name in ("cfg4a_deep_1x1", "cfg4b_small_3x3", "resnet_s5_3x3", "resnet_s4_down"):
+        assert table[name].select() == "splitk", name
 
 
 def test_dispatch_needs_a_single_wave_split():
