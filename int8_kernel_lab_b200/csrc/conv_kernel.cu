@@ -594,6 +594,16 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
       const uint32_t idesc_part = idesc_s8(kTileRows, g.bn / g.split_f);
       constexpr Layout kLayout = SwizzleOf<CBLK>::kLayout;
       constexpr uint32_t kAtom = 8 * CBLK;  // 8 rows x CBLK bytes
+      // Shared-memory descriptors are built once: moving the operand start by
+      // d bytes adds d >> 4 to the descriptor's 14-bit start-address field
+      // (operand addresses stay below 256 KB, so nothing carries out of it).
+      // One add per MMA instead of a full rebuild keeps the issuing thread
+      // ahead of the tensor pipe (a rebuilt pair of descriptors cost the
+      // thread about 70 cycles per 128-cycle MMA on B200).
+      const uint64_t a_desc0 = smem_desc(smem_u32(a_ring), 16, kAtom, kLayout);
+      const uint64_t b_desc0 = smem_desc(smem_u32(b_ring), 16, kAtom, kLayout);
+      const uint32_t a_step = plan.a_bytes >> 4;
+      const uint32_t b_step = plan.b_bytes >> 4;
       Ring ra, rb;
       int acc = 0;
       uint32_t acc_phase = 0;
@@ -619,7 +629,7 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
               ok = false;
               break;
             }
-            const uint32_t a_addr = smem_u32(a_ring + ra.stage * plan.a_bytes);
+            const uint64_t a_desc = a_desc0 + ra.stage * a_step;
             for (int t = 0; t < taps; ++t) {
               // Tap t reads the staged tile `shift` rows further on: filter
               // column s for a strip; r*dh*Wp + s*dw for a halo tile.
@@ -630,11 +640,11 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
                 break;
               }
               tc_fence_after();
-              const uint32_t b_addr = smem_u32(b_ring + rb.stage * plan.b_bytes);
+              const uint64_t ad = a_desc + ((shift * CBLK) >> 4);
+              const uint64_t bd = b_desc0 + rb.stage * b_step;
 #pragma unroll
               for (int k = 0; k < CBLK / 32; ++k) {
-                mma(d_tmem, smem_desc(a_addr + shift * CBLK + 32 * k, 16, kAtom, kLayout),
-                    smem_desc(b_addr + 32 * k, 16, kAtom, kLayout), accumulate);
+                mma(d_tmem, ad + 2 * k, bd + 2 * k, accumulate);  // +32 bytes per MMA
                 accumulate = 1;
               }
               commit_to<PAIR>(&b_empty[rb.stage]);
@@ -651,12 +661,11 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
               break;
             }
             tc_fence_after();
-            const uint32_t a_addr = smem_u32(a_ring + rb.stage * plan.a_bytes);
-            const uint32_t b_addr = smem_u32(b_ring + rb.stage * plan.b_bytes);
+            const uint64_t ad = a_desc0 + rb.stage * a_step;
+            const uint64_t bd = b_desc0 + rb.stage * b_step;
 #pragma unroll
             for (int k = 0; k < CBLK / 32; ++k) {
-              mma(d_tmem, smem_desc(a_addr + 32 * k, 16, kAtom, kLayout),
-                  smem_desc(b_addr + 32 * k, 16, kAtom, kLayout), accumulate);
+              mma(d_tmem, ad + 2 * k, bd + 2 * k, accumulate);  // +32 bytes per MMA
               accumulate = 1;
             }
             commit_to<PAIR>(&b_empty[rb.stage]);

@@ -81,10 +81,25 @@ __device__ __forceinline__ bool mbar_test_parity(uint64_t *bar, uint32_t parity)
   return done != 0;
 }
 
+// Non-blocking test of the same condition (no suspend window): the fast path
+// of a wait whose phase has usually completed already.
+__device__ __forceinline__ bool mbar_done(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Waits for the phase with parity `parity` to complete.  Returns false (and
 // sets `bit` in the status word) once the wait has lasted ctx.limit_ns.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, const WaitCtx &ctx,
                                           uint32_t bit) {
+  if (mbar_done(bar, parity)) return true;
   if (mbar_test_parity(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {

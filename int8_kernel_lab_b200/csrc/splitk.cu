@@ -163,6 +163,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       const uint32_t idesc = idesc_s8(kBlockM, g.bn);
       constexpr Layout kLayout = SplitSwizzle<CBLK>::kLayout;
       constexpr uint32_t kAtom = 8 * CBLK;
+      // Descriptors built once; a byte offset d adds d >> 4 (see conv_kernel).
+      const uint64_t a_desc0 = smem_desc(smem_u32(a_ring), 16, kAtom, kLayout);
+      const uint64_t b_desc0 = smem_desc(smem_u32(b_ring), 16, kAtom, kLayout);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t accumulate = 0;
@@ -173,12 +176,11 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(a_ring + stage * a_bytes);
-        const uint32_t b_addr = smem_u32(b_ring + stage * b_bytes);
+        const uint64_t ad = a_desc0 + ((stage * a_bytes) >> 4);
+        const uint64_t bd = b_desc0 + ((stage * b_bytes) >> 4);
 #pragma unroll
         for (int k = 0; k < CBLK / 32; ++k) {
-          umma_i8(tmem_base, smem_desc(a_addr + 32 * k, 16, kAtom, kLayout),
-                  smem_desc(b_addr + 32 * k, 16, kAtom, kLayout), idesc, accumulate);
+          umma_i8(tmem_base, ad + 2 * k, bd + 2 * k, idesc, accumulate);  // +32 bytes per MMA
           accumulate = 1;
         }
         umma_commit(&empty[stage]);
