@@ -49,6 +49,10 @@ struct ConvGeom {
   // GATHER: k-blocks whose copies may still be in flight when the next one
   // is issued (1..3, fewer than `stages`).
   int32_t gather_lag;
+  // GATHER with unit horizontal dilation: a k-block is 128 contiguous bytes
+  // of one filter row's S*C span (several taps of a small C at once) instead
+  // of one tap's channel block; `cblocks` = ceil(S*C / 128) per filter row.
+  int32_t row_blocks;
 };
 
 // Failure-detection controls passed to every kernel.

@@ -218,6 +218,7 @@ __device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t 
   const int row_base = 32 * gw;               // this warp's rows of the tile
   const int lag = g.gather_lag;
   const bool loads_filter = gw == 0 && lane == 0;
+  const bool row_blocks = g.row_blocks != 0;
   int4 *mytab = rowtab + row_base;
   Ring rb;           // next stage to fill
   Ring rp;           // oldest stage filled but not yet published
@@ -264,17 +265,31 @@ __device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t 
       }
       if (!ctl.starve) {
         if (loads_filter) {
+          // Row k-blocks read the filter viewed as [K][R][S*C] (coordinate r),
+          // tap k-blocks as [K][R*S][C] (coordinate tap).
           mbar_arrive_expect_tx(&b_full[rb.stage], plan.b_bytes);
-          tma_load_3d(b_ring + rb.stage * plan.b_bytes, tmap_w, &b_full[rb.stage], cb * CBLK, tap,
-                      t.n0);
+          tma_load_3d(b_ring + rb.stage * plan.b_bytes, tmap_w, &b_full[rb.stage], cb * CBLK,
+                      row_blocks ? r : tap, t.n0);
           ++armed_b;
         }
         const uint32_t a_base = smem_u32(a_ring + rb.stage * plan.a_bytes);
         const int dy = r * g.dil_h;
-        const int dx = s * g.dil_w;
-        const int c_off = cb * CBLK + chunk * 16;
-        const bool c_ok = c_off < g.C;
-        const int64_t tap_off = (static_cast<int64_t>(dy) * g.W + dx) * g.C + c_off;
+        int dx;
+        bool c_ok;
+        int64_t tap_off;
+        if (row_blocks) {
+          // Byte o of the filter row's S*C span: tap o / C, channel o % C (a
+          // 16-byte chunk never straddles two taps: C % 16 == 0).
+          const int o = cb * CBLK + chunk * 16;
+          c_ok = o < g.S * g.C;
+          dx = o / g.C;
+          tap_off = static_cast<int64_t>(dy) * g.W * g.C + o;
+        } else {
+          dx = s * g.dil_w;
+          const int c_off = cb * CBLK + chunk * 16;
+          c_ok = c_off < g.C;
+          tap_off = (static_cast<int64_t>(dy) * g.W + dx) * g.C + c_off;
+        }
 #pragma unroll
         for (int i = 0; i < kPasses; ++i) {
           const int row = row_base + rsub + i * kRowsPerPass;
@@ -302,10 +317,14 @@ __device__ __forceinline__ void gather_producer(const ConvGeom &g, const int8_t 
       rb.next(g.stages);
       if (++cb == g.cblocks) {
         cb = 0;
-        ++tap;
-        if (++s == g.S) {
-          s = 0;
+        if (row_blocks) {
           ++r;
+        } else {
+          ++tap;
+          if (++s == g.S) {
+            s = 0;
+            ++r;
+          }
         }
       }
     }
@@ -1026,6 +1045,20 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   g.dil_w = s.dilation_w;
   g.cblocks = (s.c + cblk - 1) / cblk;
   g.kblocks = s.r * s.s * g.cblocks;
+  // The gather with unit horizontal dilation may take 128-byte k-blocks of a
+  // filter row's S*C contiguous bytes: a small C no longer pays one k-block
+  // (and its zero padding) per tap.  Taken where it stages no more bytes than
+  // per-tap blocks do.  ViT-B/16 with C = 16: 32 k-blocks of 128 bytes per
+  // tile instead of 256 of 32 (half of them zero).
+  g.row_blocks = 0;
+  const int64_t row_padded = static_cast<int64_t>(s.r) * ((s.s * s.c + 127) / 128) * 128;
+  const int64_t tap_padded = static_cast<int64_t>(g.kblocks) * cblk;
+  if (mode == kModeGather && s.dilation_w == 1 && row_padded <= tap_padded) {
+    cblk = 128;
+    g.row_blocks = 1;
+    g.cblocks = (s.s * s.c + 127) / 128;
+    g.kblocks = s.r * g.cblocks;
+  }
   // Single CTAs of GENERIC may run narrower N tiles (i8c_generic_bn).
   const int bn_align = out_kind == kOutInt8VectC ? 32 : 16;
   g.bn = gemm_rows && !pair ? i8c_generic_bn(&s, bn_align, slots) : i8c_pick_bn(s.k, bn_align);
@@ -1124,7 +1157,8 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
     st = activation_map_im2col(s, x, CBLK, pixels, count_w, count_h, &maps[0]);
     if (st != INT8CONV_OK) return st;
   }
-  st = filter_map_tiled(s, w, CBLK, b_rows, &maps[1]);
+  st = g.row_blocks ? filter_map_rows(s, w, CBLK, b_rows, &maps[1])
+                    : filter_map_tiled(s, w, CBLK, b_rows, &maps[1]);
   if (st != INT8CONV_OK) return st;
   maps[2] = CUtensorMap{};
   if (g.tma_store) {

@@ -282,6 +282,26 @@ int8conv_status filter_map_tiled(const int8conv_shape &s, const int8_t *w, int c
   return INT8CONV_OK;
 }
 
+int8conv_status filter_map_rows(const int8conv_shape &s, const int8_t *w, int channels, int rows,
+                                CUtensorMap *map) {
+  const MapKey key = make_key(5, s, w, channels, rows, 0);
+  if (map_lookup(key, map)) return INT8CONV_OK;
+  std::call_once(g_driver_once, load_driver_entry_points);
+  if (!g_encode_tiled) return INT8CONV_CUDA_ERROR;
+  const uint64_t row_bytes = static_cast<uint64_t>(s.s) * s.c;
+  cuuint64_t dims[3] = {(cuuint64_t)row_bytes, (cuuint64_t)s.r, (cuuint64_t)s.k};
+  cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)row_bytes * s.r};
+  cuuint32_t box[3] = {(cuuint32_t)channels, 1, (cuuint32_t)rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult rc = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(w),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               swizzle_for(channels), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (rc != CUDA_SUCCESS) return INT8CONV_CUDA_ERROR;
+  map_store(key, *map);
+  return INT8CONV_OK;
+}
+
 int8conv_status output_map_tiled(int32_t *y, int64_t m, int k, CUtensorMap *map) {
   int8conv_shape key_shape{};
   key_shape.n = static_cast<int32_t>(m);

@@ -56,6 +56,12 @@ int8conv_status activation_map_im2col(const int8conv_shape &s, const int8_t *x, 
 int8conv_status filter_map_tiled(const int8conv_shape &s, const int8_t *w, int channels,
                                  int rows, CUtensorMap *map);
 
+// Tiled tensor map over the KRSC filter viewed as [K][R][S*C] (each filter
+// row's S*C bytes contiguous), box (channels, 1, rows): the gather staging's
+// row k-blocks.
+int8conv_status filter_map_rows(const int8conv_shape &s, const int8_t *w, int channels, int rows,
+                                CUtensorMap *map);
+
 // Tiled tensor map over the NHWK int32 output viewed as [M][K], box 32 x 32,
 // 128-byte swizzle (the epilogue's staging layout).
 int8conv_status output_map_tiled(int32_t *y, int64_t m, int k, CUtensorMap *map);

@@ -209,3 +209,51 @@ def test_gather_through_host_buffers(cuda):
     s.synchronize()
     assert m.device_status() == _abi.OK
     assert np.array_equal(hy.numpy(), pyoracle.conv(shape, x, w, b))
+
+
+def _channel_block(c):
+    """Host copy of i8c_channel_block (include/int8conv_rules.h)."""
+    best, best_cost, best_pad = 32, -1, 0
+    cb = 128
+    while cb >= 32:
+        blocks = -(-c // cb)
+        cost, pad = blocks * (cb + 128), blocks * cb - c
+        if best_cost < 0 or cost < best_cost or (cost == best_cost and pad < best_pad):
+            best, best_cost, best_pad = cb, cost, pad
+        cb //= 2
+    return best
+
+
+def _stages_filter_rows(shape):
+    """True where the gather stages 128-byte k-blocks of a filter row's S*C
+    span instead of per-tap channel blocks (unit horizontal dilation, no more
+    bytes staged than per-tap blocks)."""
+    cb = _channel_block(shape.c)
+    rows = shape.r * -(-(shape.s * shape.c) // 128) * 128
+    taps = shape.r * shape.s * -(-shape.c // cb) * cb
+    return shape.dilation_w == 1 and rows <= taps
+
+
+ROW_BLOCK_SHAPES = {
+    # S*C = 80: one 128-byte block per filter row, 48 bytes of it past the row.
+    "c16_5x5": m.ConvShape(4, 30, 31, 16, 72, 5, 5, 2, 2, 1, 1, 1, 1),
+    # S*C = 336: three blocks per row, the last one ragged; vertical dilation.
+    "c48_7x7_dh2": m.ConvShape(2, 41, 37, 48, 100, 7, 7, 5, 3, 2, 1, 2, 1),
+    # S*C = 240 with C = 80 (32-byte channel blocks per tap would pad to 96).
+    "c80_3x3": m.ConvShape(3, 19, 23, 80, 63, 3, 3, 1, 1, 1, 1, 1, 1),
+    # Patch embed, S*C = 256: two full blocks per row.
+    "patch16_c16": m.ConvShape(3, 96, 80, 16, 192, 16, 16, 0, 0, 16, 16, 1, 1),
+    # Taps straddle the right edge and the padding on both sides.
+    "c16_11x11_s9": m.ConvShape(2, 50, 47, 16, 40, 11, 11, 6, 9, 9, 9, 1, 1),
+}
+
+
+@pytest.mark.parametrize("name", sorted(ROW_BLOCK_SHAPES))
+def test_filter_row_blocks_match_oracle(cuda, forced_gather, name):
+    shape = ROW_BLOCK_SHAPES[name]
+    assert _stages_filter_rows(shape), name
+    x, w, b = m.make_inputs(shape, seed=71)
+    want = pyoracle.conv(shape, x, w, b)
+    got = _run(cuda, "generic", shape, x, w, b)
+    bad = np.count_nonzero(got != want)
+    assert bad == 0, f"{name}: {bad} mismatches"
