@@ -70,13 +70,20 @@ PlanSlot &plan_slot(const PlanKey &key) {
   return t_plans[(h >> 32) % kPlanSlots];
 }
 
-// Replays a cached plan, or runs `launch` (the family launcher) with plan
-// capture on and caches what it launched.
-template <class Launch>
-int8conv_status launch_cached(const PlanKey &key, cudaStream_t stream, Launch launch) {
+// The cached plan of an earlier successful launch with exactly this key, or
+// nullptr.  Every argument check of a launch depends on the key's fields
+// alone (device, family as requested, shape, buffers, pairing, staging,
+// epilogue), so a launch that finds its plan skips them.
+i8c::LaunchPlan *cached_plan(const PlanKey &key) {
   PlanSlot &slot = plan_slot(key);
-  if (slot.used && memcmp(&slot.key, &key, sizeof(PlanKey)) == 0)
-    return i8c::launch_plan(slot.plan, stream);
+  return slot.used && memcmp(&slot.key, &key, sizeof(PlanKey)) == 0 ? &slot.plan : nullptr;
+}
+
+// Runs `launch` (the family launcher) with plan capture on and caches what it
+// launched under `key`.
+template <class Launch>
+int8conv_status launch_cached(const PlanKey &key, Launch launch) {
+  PlanSlot &slot = plan_slot(key);
   i8c::LaunchPlan plan;
   i8c::plan_capture_begin(&plan);
   const int8conv_status st = launch();
@@ -98,6 +105,15 @@ bool family_built(int strategy) {
 int8conv_status launch_family(int strategy, const int8conv_shape *shape, const int8_t *input,
                               const int8_t *filter, const int32_t *bias, int32_t *output,
                               void *workspace, size_t workspace_bytes, void *stream) {
+  if (shape == nullptr) return INT8CONV_BAD_SHAPE;
+  (void)workspace;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const PlanKey key = plan_key(strategy, *shape, input, filter, bias, output, 0, nullptr);
+  if (i8c::LaunchPlan *plan = cached_plan(key)) {
+    if (workspace_bytes < int8conv_workspace_bytes(shape, strategy))
+      return INT8CONV_WORKSPACE_TOO_SMALL;
+    return i8c::launch_plan(*plan, st);
+  }
   if (!i8c_shape_valid(shape)) return INT8CONV_BAD_SHAPE;
   if (strategy == INT8CONV_AUTO) strategy = int8conv_select(shape);
   if (strategy < 0 || strategy >= INT8CONV_NUM_STRATEGIES) return INT8CONV_BAD_ARGUMENT;
@@ -106,12 +122,9 @@ int8conv_status launch_family(int strategy, const int8conv_shape *shape, const i
     return INT8CONV_BAD_POINTER;
   if (workspace_bytes < int8conv_workspace_bytes(shape, strategy))
     return INT8CONV_WORKSPACE_TOO_SMALL;
-  (void)workspace;
   const int8conv_status dev = i8c::check_device();
   if (dev != INT8CONV_OK) return dev;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const PlanKey key = plan_key(strategy, *shape, input, filter, bias, output, 0, nullptr);
-  return launch_cached(key, st, [&]() -> int8conv_status {
+  return launch_cached(key, [&]() -> int8conv_status {
     switch (strategy) {
       case INT8CONV_GENERIC:
         return i8c::launch_generic_impl(*shape, input, filter, bias, output, st);
@@ -277,8 +290,18 @@ int8conv_status int8conv_launch_requant(int strategy, const int8conv_shape *shap
                                         const int32_t *bias, const int8conv_requant *requant,
                                         int8_t *output, void *workspace, size_t workspace_bytes,
                                         void *stream) {
-  if (!i8c_shape_valid(shape)) return INT8CONV_BAD_SHAPE;
+  if (shape == nullptr) return INT8CONV_BAD_SHAPE;
   if (requant == nullptr) return INT8CONV_BAD_ARGUMENT;
+  (void)workspace;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const PlanKey key = plan_key(strategy, *shape, input, filter, bias, output,
+                               1 + requant->layout, requant);
+  if (i8c::LaunchPlan *plan = cached_plan(key)) {
+    if (workspace_bytes < int8conv_workspace_bytes(shape, strategy))
+      return INT8CONV_WORKSPACE_TOO_SMALL;
+    return i8c::launch_plan(*plan, st);
+  }
+  if (!i8c_shape_valid(shape)) return INT8CONV_BAD_SHAPE;
   if (requant->layout != INT8CONV_LAYOUT_NHWC && requant->layout != INT8CONV_LAYOUT_NCHW_VECT_C)
     return INT8CONV_BAD_ARGUMENT;
   if (requant->zero_point < -128 || requant->zero_point > 127) return INT8CONV_BAD_ARGUMENT;
@@ -293,15 +316,11 @@ int8conv_status int8conv_launch_requant(int strategy, const int8conv_shape *shap
     return INT8CONV_BAD_POINTER;
   if (workspace_bytes < int8conv_workspace_bytes(shape, strategy))
     return INT8CONV_WORKSPACE_TOO_SMALL;
-  (void)workspace;
   const int8conv_status dev = i8c::check_device();
   if (dev != INT8CONV_OK) return dev;
   const i8c::Requant rq{requant->multiplier, requant->exponent, requant->zero_point,
                         requant->relu, requant->layout};
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const PlanKey key =
-      plan_key(strategy, *shape, input, filter, bias, output, 1 + requant->layout, requant);
-  return launch_cached(key, st, [&]() -> int8conv_status {
+  return launch_cached(key, [&]() -> int8conv_status {
     if (strategy == INT8CONV_SPLITK)
       return i8c::launch_splitk_requant(*shape, input, filter, bias, rq, output, st);
     return i8c::launch_conv_requant(strategy, *shape, input, filter, bias, rq, output, st);

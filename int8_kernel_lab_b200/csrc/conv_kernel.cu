@@ -1188,7 +1188,7 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   lp.block = dim3(kernel_threads<MODE, REQ>(), 1, 1);
   lp.smem = smem_bytes;
   lp.cluster = PAIR ? 2 : 1;
-  plan_args(lp, maps[0], maps[1], maps[2], g, x, b, static_cast<int32_t *>(y), RunCtl{}, rq);
+  plan_args(lp, maps[0], maps[1], maps[2], g, x, b, static_cast<int32_t *>(y), run_ctl(), rq);
   return launch_plan(lp, stream);
 }
 

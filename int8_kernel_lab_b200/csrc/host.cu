@@ -174,8 +174,15 @@ void plan_capture_end() { t_capture = nullptr; }
 
 int8conv_status launch_plan(LaunchPlan &plan, cudaStream_t stream) {
   if (plan.ctl_arg >= 0) {
-    const RunCtl ctl = run_ctl();
-    memcpy(plan.blob + plan.offset[plan.ctl_arg], &ctl, sizeof(ctl));
+    // The status word's address is the plan device's (fixed per device); the
+    // wait limit and the starve hook are re-read at every launch.
+    RunCtl ctl;
+    unsigned char *at = plan.blob + plan.offset[plan.ctl_arg];
+    memcpy(&ctl, at, sizeof(ctl));
+    if (ctl.status == nullptr) ctl.status = device_info().status;
+    ctl.wait_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+    ctl.starve = g_starve.load(std::memory_order_relaxed);
+    memcpy(at, &ctl, sizeof(ctl));
   }
   if (t_capture != nullptr) *t_capture = plan;
   void *args[12];

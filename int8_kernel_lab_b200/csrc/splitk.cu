@@ -406,7 +406,7 @@ static int8conv_status launch_split_t(const int8conv_shape &s, const SplitGeom &
   plan.block = dim3(kSplitThreads, 1, 1);
   plan.smem = smem;
   plan.cluster = sg.splits;
-  plan_args(plan, maps[0], maps[1], sg, b, static_cast<int32_t *>(y), RunCtl{}, rq);
+  plan_args(plan, maps[0], maps[1], sg, b, static_cast<int32_t *>(y), run_ctl(), rq);
   return launch_plan(plan, stream);
 }
 
