@@ -185,18 +185,17 @@ I8C_RULE int32_t i8c_pick_split(int64_t num_tiles, int32_t slots, int32_t bn) {
   return best_f;
 }
 
-/* GENERIC's N-tile width for single CTAs with `slots` of them resident.  A
- * layer whose 128-row tiles fill less than one wave, and whose width is not
- * a multiple of 64 (so tail balancing cannot cut it into column parts), runs
- * narrower N tiles instead, as many as the span model asks for.  A narrow
- * tile loads only its own filter rows, while each column part of a wide tile
- * would load the whole filter box (B200, K = 100 on 25 row tiles: four
- * 32-column tiles 13.4-14.1 us per launch against 16.2 us for one 112-column
- * tile and 16.2 us for four parts of a 128-column tile). */
-I8C_RULE int32_t i8c_generic_bn(const int8conv_shape *s, int32_t align, int32_t slots) {
-  int32_t bn = i8c_pick_bn(s->k, align);
-  const int64_t m_tiles = ((int64_t)s->n * i8c_out_h(s) * i8c_out_w(s) + 127) / 128;
-  const int64_t tiles = m_tiles * ((s->k + bn - 1) / bn);
+/* N-tile width for single CTAs with `slots` of them resident, over `m_tiles`
+ * 128-row tiles.  A layer whose tiles fill less than one wave, and whose
+ * width is not a multiple of 64 (so tail balancing cannot cut it into column
+ * parts), runs narrower N tiles instead, as many as the span model asks for.
+ * A narrow tile loads only its own filter rows, while each column part of a
+ * wide tile would load the whole filter box (B200, K = 100 on 25 row tiles:
+ * four 32-column tiles 13.4-14.1 us per launch against 16.2 us for one
+ * 112-column tile and 16.2 us for four parts of a 128-column tile). */
+I8C_RULE int32_t i8c_narrow_bn(int32_t k, int32_t align, int64_t m_tiles, int32_t slots) {
+  int32_t bn = i8c_pick_bn(k, align);
+  const int64_t tiles = m_tiles * ((k + bn - 1) / bn);
   if (slots > 0 && tiles < slots && i8c_pick_split(tiles, slots, bn) == 1) {
     const int32_t f = i8c_pick_split(tiles, slots, 0);
     if (f > 1) {
@@ -206,6 +205,12 @@ I8C_RULE int32_t i8c_generic_bn(const int8conv_shape *s, int32_t align, int32_t 
     }
   }
   return bn;
+}
+
+/* GENERIC's N-tile width for single CTAs: its rows are the output pixels. */
+I8C_RULE int32_t i8c_generic_bn(const int8conv_shape *s, int32_t align, int32_t slots) {
+  const int64_t m_tiles = ((int64_t)s->n * i8c_out_h(s) * i8c_out_w(s) + 127) / 128;
+  return i8c_narrow_bn(s->k, align, m_tiles, slots);
 }
 
 /* HALO: positions run over the zero-padded image (Hp x Wp, Hp = out_h +

@@ -1059,9 +1059,20 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
     g.cblocks = (s.s * s.c + 127) / 128;
     g.kblocks = s.r * g.cblocks;
   }
-  // Single CTAs of GENERIC may run narrower N tiles (i8c_generic_bn).
+  // Single CTAs may run narrower N tiles (i8c_narrow_bn) over their row
+  // tiles: output pixels (GENERIC), or positions of the padded grid (STRIP:
+  // out_h x Wp per image; HALO: Hp x Wp).
   const int bn_align = out_kind == kOutInt8VectC ? 32 : 16;
-  g.bn = gemm_rows && !pair ? i8c_generic_bn(&s, bn_align, slots) : i8c_pick_bn(s.k, bn_align);
+  if (pair) {
+    g.bn = i8c_pick_bn(s.k, bn_align);
+  } else if (gemm_rows) {
+    g.bn = i8c_generic_bn(&s, bn_align, slots);
+  } else {
+    const int64_t wp = out_w + static_cast<int64_t>(s.s - 1) * s.dilation_w;
+    const int64_t hp = mode == kModeHalo ? out_h + static_cast<int64_t>(s.r - 1) * s.dilation_h
+                                         : out_h;
+    g.bn = i8c_narrow_bn(s.k, bn_align, (s.n * hp * wp + kBlockM - 1) / kBlockM, slots);
+  }
   g.pair = pair ? 1 : 0;
   g.acc_stride = (g.bn + 31) / 32 * 32;
   g.tmem_cols = next_pow2(2 * g.acc_stride);
