@@ -434,25 +434,25 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
   const int tile_first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int tile_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < a_stages; ++i) {
-      mbar_init(&a_full[i], 1);
-      mbar_init(&a_empty[i], 1);
-    }
-    for (int i = 0; i < g.stages; ++i) {
+  if (warp == 0) {
+    // The barriers are contiguous (a_full, a_empty, b_full, b_empty, tfull,
+    // tempty, drain); lane i initialises barriers i, i + 32, ...  One thread
+    // initialising all of them in sequence held up the first loads of the
+    // small layers by about 0.3 us on B200.
+    const int n_ab = 2 * a_stages + 2 * g.stages;
+    for (int i = lane; i < n_ab + 5; i += 32) {
+      uint32_t count = 1;
       // GATHER: the filter load's arrival plus one per gather lane.
-      mbar_init(&b_full[i], GATHER ? 1 + 32 * kGatherWarps : 1);
-      mbar_init(&b_empty[i], 1);
+      if (GATHER && i >= 2 * a_stages && i < 2 * a_stages + g.stages) count = 1 + 32 * kGatherWarps;
+      // tempty: one arrival per epilogue warp (of both CTAs for a pair).
+      if (i >= n_ab + 2 && i < n_ab + 4) count = (PAIR ? 2 : 1) * epilogue_warps<REQ>();
+      mbar_init(&a_full[i], count);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&tfull[i], 1);
-      // One arrival per epilogue warp (of both CTAs for a pair).
-      mbar_init(&tempty[i], (PAIR ? 2 : 1) * epilogue_warps<REQ>());
-    }
-    mbar_init(drain, 1);
     fence_mbar_init();
-    if constexpr (!GATHER) tma_prefetch_desc(&tmap_x);
-    tma_prefetch_desc(&tmap_w);
+    if (lane == 0) {
+      if constexpr (!GATHER) tma_prefetch_desc(&tmap_x);
+      tma_prefetch_desc(&tmap_w);
+    }
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -470,13 +470,15 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Launched with programmatic stream serialisation: the set-up above may run
-  // while the previous kernel in the stream finishes; no thread reads or
-  // writes global memory before that kernel is complete.
-  griddep_wait();
-  griddep_launch_dependents();
+  // while the previous kernel in the stream finishes.  Each role that reads
+  // or writes global memory (the producers, the epilogue warps) waits for
+  // that kernel to complete before its first access (griddep_wait); the MMA
+  // issuer touches only shared memory and TMEM.  The first epilogue warp lets
+  // the next kernel's set-up start.
 
   constexpr int kFirstExtraGather = 2 + epilogue_warps<REQ>();
   if (GATHER && (warp == 0 || warp >= kFirstExtraGather)) {
+    griddep_wait();
     gather_producer<CBLK>(g, x, &tmap_w, a_ring, b_ring, plan,
                           reinterpret_cast<int4 *>(smem + plan.rows_off), b_full, b_empty, ctl,
                           wctx, tile_first, tile_step,
@@ -484,6 +486,7 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
   } else if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
+      griddep_wait();
       Ring ra, rb;
       long armed_a = 0, armed_b = 0;
       const uint32_t a_tx = (SHIFT ? g.strip_px : kBlockM) * CBLK;
@@ -628,6 +631,12 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       uint32_t idesc = idesc_full;
+      // A CTA with a single tile whose k-blocks (and staged A tiles) fit the
+      // rings never refills a stage, so its MMAs release none (a commit costs
+      // the issuing thread about as much as an MMA).
+      const int a_used = STRIP ? g.R * g.cblocks : g.cblocks;
+      const bool refill = tile_first + tile_step < g.num_units || g.kblocks > g.stages ||
+                          (SHIFT && a_used > a_stages);
       auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t accumulate) {
         if constexpr (PAIR)
           umma_i8_pair(d, a, b, idesc, accumulate);
@@ -666,11 +675,11 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
                 mma(d_tmem, ad + 2 * k, bd + 2 * k, accumulate);  // +32 bytes per MMA
                 accumulate = 1;
               }
-              commit_to<PAIR>(&b_empty[rb.stage]);
+              if (refill) commit_to<PAIR>(&b_empty[rb.stage]);
               rb.next(g.stages);
             }
             if (!ok) break;
-            commit_to<PAIR>(&a_empty[ra.stage]);
+            if (refill) commit_to<PAIR>(&a_empty[ra.stage]);
             ra.next(a_stages);
           }
         } else {
@@ -687,7 +696,7 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
               mma(d_tmem, ad + 2 * k, bd + 2 * k, accumulate);  // +32 bytes per MMA
               accumulate = 1;
             }
-            commit_to<PAIR>(&b_empty[rb.stage]);
+            if (refill) commit_to<PAIR>(&b_empty[rb.stage]);
             rb.next(g.stages);
           }
         }
@@ -708,6 +717,8 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
     }
   } else if constexpr (REQ) {
     // ---------------- int8 epilogue (warps 2..17) ----------------
+    griddep_wait();
+    if (warp == 2) griddep_launch_dependents();
     constexpr int kGroups = epilogue_warps<REQ>() / 4;
     const int quarter = warp & 3;          // TMEM lane quarter this warp may access
     const int cgroup = (warp - 2) >> 2;    // 32-column blocks cgroup, cgroup + 4, ...
@@ -842,6 +853,8 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
     if (g.tma_store && lane == 0) bulk_wait_group_read_all();
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    griddep_wait();
+    if (warp == 2) griddep_launch_dependents();
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
     const bool vec_k = (g.K & 3) == 0;
