@@ -99,7 +99,7 @@ struct Options {
 [[noreturn]] void usage() {
   std::cerr << "usage: conv_lab [--strategy generic|strip|halo|splitk|both|all|auto] [--csv] "
                "[--warmup N] [--iterations N] [--case NAME] [--config CSV] "
-               "[--values full|reference] [--seed S] [--batch N] [--peak-tops T] "
+               "[--values full|reference|ones] [--seed S] [--batch N] [--peak-tops T] "
                "[--no-graph] [--pairing auto|single|pair] [--validate-samples N] "
                "[--epilogue int32|int8|int8x32] [--rotate-l2] [--staging auto|gather]\n";
   std::exit(EXIT_FAILURE);
@@ -140,7 +140,7 @@ Options parse_options(int argc, char **argv) {
   }
   const std::vector<std::string> ok = {"generic", "strip", "halo", "splitk", "both", "all", "auto"};
   if (std::find(ok.begin(), ok.end(), o.strategy) == ok.end() || o.warmup < 0 ||
-      o.iterations <= 0 || (o.values != "full" && o.values != "reference") || o.batch < 0 ||
+      o.iterations <= 0 || (o.values != "full" && o.values != "reference" && o.values != "ones") || o.batch < 0 ||
       (o.epilogue != "int32" && o.epilogue != "int8" && o.epilogue != "int8x32")) {
     std::cerr << "invalid benchmark options\n";
     std::exit(EXIT_FAILURE);
@@ -357,10 +357,15 @@ int run_lab(int argc, char **argv) {
   }
 
   // Seeded host inputs (conv_lab.cu:149-157); --values full uses the whole
-  // int8 range and a bias in [-65536, 65536].
+  // int8 range and a bias in [-65536, 65536].  --values ones sets every input
+  // and filter byte to 1: the same work with operands that barely toggle, to
+  // show how much of a layer's time the power-managed SM clock costs on
+  // random operands.
   std::mt19937 rng(options.seed);
   const bool ref_values = options.values == "reference";
-  std::uniform_int_distribution<int> values(ref_values ? -4 : -128, ref_values ? 4 : 127);
+  const bool ones = options.values == "ones";
+  std::uniform_int_distribution<int> values(ones ? 1 : ref_values ? -4 : -128,
+                                            ones ? 1 : ref_values ? 4 : 127);
   std::uniform_int_distribution<int> bias_values(ref_values ? -31 : -65536,
                                                  ref_values ? 31 : 65536);
   std::vector<int8_t> input(d.input_elements), filter(d.filter_elements);
