@@ -91,11 +91,14 @@ def parse_args():
 
 def int8_peak():
     """Roofline denominator of the conv kernel: B200's dense INT8 tensor peak,
-    4.5 POPS nominal.  The int8 tensor pipe itself, measured on this pool with
-    back-to-back kind::i8 MMAs at 1965 MHz, gives 4586 TOPS (98 % of nominal),
-    so the nominal figure is the tighter of the two."""
+    4.5 POPS nominal.  The int8 tensor pipe itself (lib/mma_ceiling:
+    back-to-back kind::i8 MMAs, no memory traffic) retires 16 384 ops per
+    clock per SM: 4.59 POPS at 1.9 GHz with zero operands, 3.88 POPS at
+    1.61 GHz with random ones held for 115 ms, so the nominal figure is the
+    tighter of the two."""
     return NOMINAL_INT8_TOPS, ("B200 dense INT8 nominal 4.5 POPS (the int8 tensor pipe "
-                               "measures 4586 TOPS at 1965 MHz on this pool)")
+                               "retires 16384 ops/clk/SM: 4.59 POPS at 1.9 GHz, zero "
+                               "operands; 3.88 POPS at 1.61 GHz, random operands)")
 
 
 def bf16_peaks():
