@@ -39,6 +39,24 @@ def _stream(stream) -> int:
     return int(stream.cuda_stream)
 
 
+def _check_device(*tensors) -> None:
+    """Every launch runs on the current CUDA device.  A buffer that lives on
+    another GPU would be dereferenced there through a foreign address (an
+    illegal-address fault without peer access), so it is refused here."""
+    import torch
+
+    current = None
+    for t in tensors:
+        if t is None or isinstance(t, int) or not getattr(t, "is_cuda", False):
+            continue
+        if current is None:
+            current = torch.cuda.current_device()
+        if t.device.index != current:
+            raise ValueError(
+                f"buffer on {t.device}, but the current CUDA device is cuda:{current}: "
+                f"launch under torch.cuda.device({t.device.index}) or move the buffers")
+
+
 def _check_tensors(shape: ConvShape, x, w, b, y) -> None:
     import torch
 
@@ -54,6 +72,7 @@ def _check_tensors(shape: ConvShape, x, w, b, y) -> None:
             raise ValueError(
                 f"{name}: expected a contiguous CUDA {dtype} tensor of {count} elements, "
                 f"got {t.dtype} {tuple(t.shape)} on {t.device}")
+    _check_device(x, w, b, y)
 
 
 def launch(strategy: str, shape: ConvShape, x, w, b, y, *, workspace=None,
@@ -153,6 +172,7 @@ def launch_requant(strategy: str, shape: ConvShape, x, w, b, multiplier, exponen
             raise ValueError(
                 f"{name}: expected a contiguous CUDA {dtype} tensor of {count} elements, "
                 f"got {t.dtype} {tuple(t.shape)} on {t.device}")
+    _check_device(x, multiplier, exponent, y)
     rq = _abi.CRequant(_ptr(multiplier), _ptr(exponent), int(zero_point), 1 if relu else 0,
                        _abi.LAYOUTS[layout])
     status = _abi.lib.int8conv_launch_requant(

@@ -97,3 +97,47 @@ def test_row_count_bound_leaves_a_tile_of_slack():
     for w in (8388606, 8388607):  # 2^31 - 512, 2^31 - 256 rows
         big = m.ConvShape(1, 256, w, 16, 16, 1, 1, 0, 0, 1, 1, 1, 1)
         assert big.n * big.h * big.w < 2**31 and not big.valid
+
+
+class _FakeCudaTensor:
+    """Stands in for a CUDA tensor on another GPU (no GPU needed)."""
+
+    def __init__(self, dtype, count, index):
+        import torch
+
+        self.is_cuda = True
+        self.dtype = dtype
+        self.shape = (count,)
+        self.device = torch.device("cuda", index)
+        self._count = count
+
+    def is_contiguous(self):
+        return True
+
+    def numel(self):
+        return self._count
+
+    def data_ptr(self):
+        return 1 << 20
+
+
+def test_buffers_on_another_device_are_refused(monkeypatch):
+    # The launch would run on the current device with pointers into another
+    # GPU's memory; the Python mirror refuses it before calling the library.
+    import torch
+
+    from int8_kernel_lab_b200 import api
+
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    s = m.load_workloads()["cfg1_smoke"]
+    x = _FakeCudaTensor(torch.int8, s.input_elements, 1)
+    w = _FakeCudaTensor(torch.int8, s.filter_elements, 1)
+    b = _FakeCudaTensor(torch.int32, s.k, 1)
+    y = _FakeCudaTensor(torch.int32, s.output_elements, 1)
+    with pytest.raises(ValueError, match="current CUDA device is cuda:0"):
+        api.launch("generic", s, x, w, b, y)
+    with pytest.raises(ValueError, match="current CUDA device"):
+        api.launch_generic(s, x, w, b, y)
+    # Same device: the check passes (the launch itself is not reached here).
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 1)
+    api._check_tensors(s, x, w, b, y)
