@@ -53,6 +53,12 @@ struct ConvGeom {
   // of one filter row's S*C span (several taps of a small C at once) instead
   // of one tap's channel block; `cblocks` = ceil(S*C / 128) per filter row.
   int32_t row_blocks;
+  // STRIP with TMA output stores: the number of output tensor maps, map i
+  // with a box of 32 - i rows.  An epilogue block of 32 padded positions
+  // holds 32 - i valid ones (consecutive output pixels); staged compactly,
+  // they leave as one store through map i.  Blocks with fewer valid
+  // positions (the grid's tail) use 16-byte stores.
+  int32_t store_maps;
 };
 
 // Failure-detection controls passed to every kernel.

@@ -21,10 +21,13 @@
 //   warps 2-5  epilogue: tcgen05.ld (one output pixel row per thread),
 //              + bias, a 32 x 32 int32 block staged in 128-byte-swizzled
 //              shared memory and written by one TMA tensor store (rows >= M
-//              and columns >= K clipped).  Where a TMA store does not apply
-//              (STRIP/HALO padded rows, K % 4 != 0, a block crossing into
-//              the next N tile) the staged block is transposed and leaves as
-//              16-byte stores that write whole 128-byte row segments.
+//              and columns >= K clipped).  STRIP stages only a block's
+//              valid rows (consecutive output pixels), compacted, and stores
+//              them through the map whose box has that many rows.  Where a
+//              TMA store does not apply (HALO padded rows, K % 4 != 0, a
+//              block crossing into the next N tile) the staged block is
+//              transposed and leaves as 16-byte stores that write whole
+//              128-byte row segments.
 //   warps 2-17 with the requantised int8 epilogue (REQ): four warps per TMEM
 //              lane quarter, each owning every fourth 32-column block;
 //              per-N-tile channel tables in shared memory; 32 x 32-byte TMA
@@ -390,11 +393,29 @@ constexpr int kernel_threads() {
   return 64 + 32 * epilogue_warps<REQ>() + (MODE == kModeGather ? 32 * (kGatherWarps - 1) : 0);
 }
 
+// Output tensor maps of a launch.  GENERIC and the gather staging: one map
+// over NHWK viewed as [M][K], box 32 x 32.  STRIP with the int32 epilogue:
+// maps of the same view with boxes of 32, 31, ... rows (ConvGeom::store_maps
+// of them), one store per epilogue block of its valid rows, staged compactly.
+constexpr int kMaxStoreMaps = 8;
+struct alignas(64) StripOutMaps {
+  CUtensorMap rows[kMaxStoreMaps];
+};
+template <int MODE, bool REQ>
+struct OutMaps {
+  using type = CUtensorMap;
+};
+template <>
+struct OutMaps<kModeStrip, false> {
+  using type = StripOutMaps;
+};
+
 template <int CBLK, int MODE, bool PAIR, bool REQ>
 __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
     conv_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_w,
-                const __grid_constant__ CUtensorMap tmap_y, const ConvGeom g,
+                const __grid_constant__ typename OutMaps<MODE, REQ>::type tmap_y,
+                const ConvGeom g,
                 const int8_t *__restrict__ x, const int32_t *__restrict__ bias,
                 int32_t *__restrict__ out, const RunCtl ctl, const Requant rq) {
   extern __shared__ uint8_t smem_raw[];
@@ -650,37 +671,49 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * g.acc_stride);
         uint32_t accumulate = 0;
         if constexpr (SHIFT) {
-          const int groups = STRIP ? g.R * g.cblocks : g.cblocks;
+          // One flat loop over the k-blocks in the producer's order: groups
+          // (a staged tile each: filter row x channel block for a strip, a
+          // channel block for a halo tile), then the taps that share it.  Tap
+          // t reads the staged tile `shift` rows further on: filter column s
+          // for a strip; r*dh*Wp + s*dw for a halo tile, kept incrementally.
           const int taps = STRIP ? g.S : g.R * g.S;
-          for (int grp = 0; grp < groups && ok; ++grp) {
-            if (!mbar_wait(&a_full[ra.stage], ra.phase, wctx, kStatusTimeoutFull)) {
-              ok = false;
-              break;
-            }
-            const uint64_t a_desc = a_desc0 + ra.stage * a_step;
-            for (int t = 0; t < taps; ++t) {
-              // Tap t reads the staged tile `shift` rows further on: filter
-              // column s for a strip; r*dh*Wp + s*dw for a halo tile.
-              const int shift =
-                  STRIP ? t : (t / g.S) * g.dil_h * g.Wp + (t - (t / g.S) * g.S) * g.dil_w;
-              if (!mbar_wait(&b_full[rb.stage], rb.phase, wctx, kStatusTimeoutFull)) {
+          const int row_step = g.dil_h * g.Wp;
+          int t = 0, shift = 0, col = 0;
+          uint64_t a_desc = a_desc0;
+          for (int kb = 0; kb < g.kblocks; ++kb) {
+            if (t == 0) {
+              if (!mbar_wait(&a_full[ra.stage], ra.phase, wctx, kStatusTimeoutFull)) {
                 ok = false;
                 break;
               }
-              tc_fence_after();
-              const uint64_t ad = a_desc + ((shift * CBLK) >> 4);
-              const uint64_t bd = b_desc0 + rb.stage * b_step;
-#pragma unroll
-              for (int k = 0; k < CBLK / 32; ++k) {
-                mma(d_tmem, ad + 2 * k, bd + 2 * k, accumulate);  // +32 bytes per MMA
-                accumulate = 1;
-              }
-              if (refill) commit_to<PAIR>(&b_empty[rb.stage]);
-              rb.next(g.stages);
+              a_desc = a_desc0 + ra.stage * a_step;
             }
-            if (!ok) break;
-            if (refill) commit_to<PAIR>(&a_empty[ra.stage]);
-            ra.next(a_stages);
+            if (!mbar_wait(&b_full[rb.stage], rb.phase, wctx, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t ad = a_desc + ((shift * CBLK) >> 4);
+            const uint64_t bd = b_desc0 + rb.stage * b_step;
+#pragma unroll
+            for (int k = 0; k < CBLK / 32; ++k) {
+              mma(d_tmem, ad + 2 * k, bd + 2 * k, accumulate);  // +32 bytes per MMA
+              accumulate = 1;
+            }
+            if (refill) commit_to<PAIR>(&b_empty[rb.stage]);
+            rb.next(g.stages);
+            if (++t == taps) {
+              t = shift = col = 0;
+              if (refill) commit_to<PAIR>(&a_empty[ra.stage]);
+              ra.next(a_stages);
+            } else if (STRIP) {
+              shift = t;
+            } else if (++col == g.S) {
+              col = 0;
+              shift += row_step - (g.S - 1) * g.dil_w;
+            } else {
+              shift += g.dil_w;
+            }
           }
         } else {
           for (int kb = 0; kb < g.kblocks; ++kb) {
@@ -891,6 +924,18 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
         valid = valid && j < g.Q && i < g.P;
         m = (img * g.P + i) * g.Q + j;
       }
+      // STRIP: this warp's 32 positions hold `strip_v` valid ones, which are
+      // consecutive output pixels from `strip_m0` on (rows and images follow
+      // each other in NHWK); lane l stages its row at `strip_d`, its rank
+      // among the valid lanes, and the block leaves through map 32 - strip_v.
+      int strip_v = 0, strip_d = 0, strip_m0 = 0;
+      if constexpr (STRIP) {
+        const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
+        strip_v = __popc(vmask);
+        strip_d = __popc(vmask & ((1u << lane) - 1u));
+        strip_m0 = __shfl_sync(0xffffffffu, m, vmask ? __ffs(static_cast<int>(vmask)) - 1 : 0);
+      }
+      const bool strip_tma = STRIP && g.tma_store && strip_v > 0 && 32 - strip_v < g.store_maps;
       // All lanes wait; the vote keeps the warp converged for tcgen05.ld even
       // if the wait runs out on some lanes only.
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, wctx, kStatusTimeoutAccum)))
@@ -924,28 +969,64 @@ __global__ void __launch_bounds__(kernel_threads<MODE, REQ>(), 1)
           }
         }
         const int col0 = n0 + c0;
-        if (g.tma_store) {
-          int4 *stg = stg_w + (ci & 1) * 256;
-          // The store issued two blocks ago read this buffer: let it finish.
-          if (lane == 0) bulk_wait_group_read<1>();
-          __syncwarp();
+        if constexpr (STRIP) {
+          if (strip_tma) {
+            int4 *stg = stg_w + (ci & 1) * 256;
+            // The store issued two blocks ago read this buffer: let it finish.
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+            if (valid) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const bool in = c0 + 4 * j < bn && col0 + 4 * j < g.K;
-            const int4 bb =
-                in ? __ldg(reinterpret_cast<const int4 *>(bias + col0) + j) : make_int4(0, 0, 0, 0);
-            stg[lane * 8 + (j ^ (lane & 7))] = make_int4(
-                static_cast<int32_t>(v[4 * j]) + bb.x, static_cast<int32_t>(v[4 * j + 1]) + bb.y,
-                static_cast<int32_t>(v[4 * j + 2]) + bb.z, static_cast<int32_t>(v[4 * j + 3]) + bb.w);
+              for (int j = 0; j < 8; ++j) {
+                const bool in = c0 + 4 * j < bn && col0 + 4 * j < g.K;
+                const int4 bb = in ? __ldg(reinterpret_cast<const int4 *>(bias + col0) + j)
+                                   : make_int4(0, 0, 0, 0);
+                stg[strip_d * 8 + (j ^ (strip_d & 7))] = make_int4(
+                    static_cast<int32_t>(v[4 * j]) + bb.x, static_cast<int32_t>(v[4 * j + 1]) + bb.y,
+                    static_cast<int32_t>(v[4 * j + 2]) + bb.z,
+                    static_cast<int32_t>(v[4 * j + 3]) + bb.w);
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmap_y.rows[32 - strip_v], stg, col0, strip_m0);
+              bulk_commit_group();
+            }
+            ++ci;
+            continue;
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmap_y, stg, col0, row0);
-            bulk_commit_group();
+          // 16-byte stores through buffer 0: earlier TMA stores must have
+          // read it.
+          if (g.tma_store) {
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
           }
-          ++ci;
-          continue;
+        } else {
+          if (g.tma_store) {
+            int4 *stg = stg_w + (ci & 1) * 256;
+            // The store issued two blocks ago read this buffer: let it finish.
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const bool in = c0 + 4 * j < bn && col0 + 4 * j < g.K;
+              const int4 bb = in ? __ldg(reinterpret_cast<const int4 *>(bias + col0) + j)
+                                 : make_int4(0, 0, 0, 0);
+              stg[lane * 8 + (j ^ (lane & 7))] = make_int4(
+                  static_cast<int32_t>(v[4 * j]) + bb.x, static_cast<int32_t>(v[4 * j + 1]) + bb.y,
+                  static_cast<int32_t>(v[4 * j + 2]) + bb.z,
+                  static_cast<int32_t>(v[4 * j + 3]) + bb.w);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmap_y, stg, col0, row0);
+              bulk_commit_group();
+            }
+            ++ci;
+            continue;
+          }
         }
         int4 *stg = stg_w;
 #pragma unroll
@@ -1160,6 +1241,24 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
     g.tma_store = gemm_rows && s.k % 16 == 0 && (g.bn % 32 == 0 || g.n_tiles == 1);
   else
     g.tma_store = 0;
+  // STRIP, int32: every epilogue block (32 positions from a multiple of 32)
+  // drops the padded positions j >= out_w it holds; its valid ones are
+  // consecutive output pixels.  One map per possible count of dropped
+  // positions, if there are at most kMaxStoreMaps of them.
+  g.store_maps = 0;
+  if (mode == kModeStrip && out_kind == kOutInt32 && s.k % 4 == 0 &&
+      (g.bn % 32 == 0 || g.n_tiles == 1)) {
+    int most = 0;
+    for (int t = 0; t < g.Wp; ++t) {  // block starts 32 t mod Wp repeat within Wp blocks
+      int dropped = 0;
+      for (int r = 0; r < 32; ++r) dropped += (32 * t + r) % g.Wp >= g.Q ? 1 : 0;
+      if (dropped > most) most = dropped;
+    }
+    if (most + 1 <= kMaxStoreMaps) {
+      g.store_maps = most + 1;
+      g.tma_store = 1;
+    }
+  }
   return true;
 }
 
@@ -1185,10 +1284,19 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
                     : filter_map_tiled(s, w, CBLK, b_rows, &maps[1]);
   if (st != INT8CONV_OK) return st;
   maps[2] = CUtensorMap{};
-  if (g.tma_store) {
-    st = REQ ? output_map_i8(static_cast<int8_t *>(y), g.M, g.K, &maps[2])
-             : output_map_tiled(static_cast<int32_t *>(y), g.M, g.K, &maps[2]);
-    if (st != INT8CONV_OK) return st;
+  typename OutMaps<MODE, REQ>::type out_maps{};
+  if constexpr (MODE == kModeStrip && !REQ) {
+    for (int i = 0; i < g.store_maps; ++i) {
+      st = output_map_rows(static_cast<int32_t *>(y), g.M, g.K, 32 - i, &out_maps.rows[i]);
+      if (st != INT8CONV_OK) return st;
+    }
+  } else {
+    if (g.tma_store) {
+      st = REQ ? output_map_i8(static_cast<int8_t *>(y), g.M, g.K, &maps[2])
+               : output_map_tiled(static_cast<int32_t *>(y), g.M, g.K, &maps[2]);
+      if (st != INT8CONV_OK) return st;
+    }
+    out_maps = maps[2];
   }
   const SmemPlan plan =
       smem_plan(CBLK, b_rows, SHIFT ? g.a_rows : kBlockM, g.a_stages, g.stages, GATHER);
@@ -1212,7 +1320,7 @@ static int8conv_status launch_t(const int8conv_shape &s, const ConvGeom &g, cons
   lp.block = dim3(kernel_threads<MODE, REQ>(), 1, 1);
   lp.smem = smem_bytes;
   lp.cluster = PAIR ? 2 : 1;
-  plan_args(lp, maps[0], maps[1], maps[2], g, x, b, static_cast<int32_t *>(y), run_ctl(), rq);
+  plan_args(lp, maps[0], maps[1], out_maps, g, x, b, static_cast<int32_t *>(y), run_ctl(), rq);
   return launch_plan(lp, stream);
 }
 

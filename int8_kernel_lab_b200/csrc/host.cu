@@ -329,6 +329,26 @@ int8conv_status output_map_tiled(int32_t *y, int64_t m, int k, CUtensorMap *map)
   return INT8CONV_OK;
 }
 
+int8conv_status output_map_rows(int32_t *y, int64_t m, int k, int rows, CUtensorMap *map) {
+  int8conv_shape key_shape{};
+  key_shape.n = static_cast<int32_t>(m);
+  key_shape.k = k;
+  const MapKey key = make_key(6, key_shape, y, 32, rows, 0);
+  if (map_lookup(key, map)) return INT8CONV_OK;
+  std::call_once(g_driver_once, load_driver_entry_points);
+  if (!g_encode_tiled) return INT8CONV_CUDA_ERROR;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  cuuint64_t strides[1] = {(cuuint64_t)k * 4};
+  cuuint32_t box[2] = {32, (cuuint32_t)rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult rc = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, y, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (rc != CUDA_SUCCESS) return INT8CONV_CUDA_ERROR;
+  map_store(key, *map);
+  return INT8CONV_OK;
+}
+
 int8conv_status output_map_i8(int8_t *y, int64_t m, int k, CUtensorMap *map) {
   int8conv_shape key_shape{};
   key_shape.n = static_cast<int32_t>(m);

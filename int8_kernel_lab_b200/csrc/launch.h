@@ -66,6 +66,10 @@ int8conv_status filter_map_rows(const int8conv_shape &s, const int8_t *w, int ch
 // 128-byte swizzle (the epilogue's staging layout).
 int8conv_status output_map_tiled(int32_t *y, int64_t m, int k, CUtensorMap *map);
 
+// The same view with a box of 32 columns x `rows` rows (1..32), 128-byte
+// swizzle: STRIP's stores of a block's valid rows, staged compactly.
+int8conv_status output_map_rows(int32_t *y, int64_t m, int k, int rows, CUtensorMap *map);
+
 // Tiled tensor map over the NHWC int8 requantised output viewed as [M][K]
 // (K % 16 == 0), box 32 x 32, no swizzle: one epilogue warp's 32 rows x 32
 // columns per store.
@@ -93,13 +97,23 @@ struct LaunchPlan {
   int nargs = 0;
   uint16_t offset[12] = {};             // argument k lives at blob + offset[k]
   int ctl_arg = -1;                     // index of the RunCtl argument
-  alignas(64) unsigned char blob[768];  // argument values, kernel-parameter aligned
+  alignas(64) unsigned char blob[2048];  // argument values, kernel-parameter aligned
 };
+
+// Bytes the kernel arguments take when packed with their alignments.
+template <class... Args>
+constexpr size_t packed_args_size() {
+  size_t at = 0;
+  ((at = (at + alignof(Args) - 1) / alignof(Args) * alignof(Args) + sizeof(Args)), ...);
+  return at;
+}
 
 // Packs typed kernel arguments into plan->blob (their types must be the
 // kernel's parameter types, in order).
 template <class... Args>
 void plan_args(LaunchPlan &plan, const Args &...args) {
+  static_assert(packed_args_size<std::decay_t<Args>...>() <= sizeof(LaunchPlan::blob),
+                "kernel arguments exceed the plan's argument block");
   size_t at = 0;
   plan.nargs = 0;
   auto put = [&](const auto &a) {
