@@ -182,6 +182,11 @@ int int8conv_select(const int8conv_shape *shape) {
   //  * Except where GENERIC runs narrow N tiles (i8c_generic_bn): those fill
   //    the GPU without a reduction (4c, K = 100: 13.4-13.8 us per launch
   //    against 15.1-15.2 us for SPLITK, three interleaved runs on one box).
+  //    There each narrow tile stages all nine taps of its 128 rows again;
+  //    HALO stages one halo tile per row tile and channel block, so where it
+  //    is eligible it runs instead (4c: 6.11-6.16 against 6.97-7.02 us per
+  //    launch in graph replay, 13.63-13.76 against 13.66-13.79 us per
+  //    launch back to back, three interleaved runs on one box).
   if (!i8c_shape_valid(shape)) return INT8CONV_GENERIC;
   const int32_t clusters[9] = I8C_B200_CLUSTERS;
   // GENERIC's narrow-tile rule runs with the current device's SM count (the
@@ -191,7 +196,7 @@ int int8conv_select(const int8conv_shape *shape) {
   if (i8c::check_device() == INT8CONV_OK) slots = i8c::device_info().sm_count;
   if (i8c_generic_bn(shape, 16, slots) < i8c_pick_bn(shape->k, 16) &&
       int8conv_eligible(shape, INT8CONV_GENERIC))
-    return INT8CONV_GENERIC;
+    return int8conv_eligible(shape, INT8CONV_HALO) ? INT8CONV_HALO : INT8CONV_GENERIC;
   const int64_t m = static_cast<int64_t>(shape->n) * i8c_out_h(shape) * i8c_out_w(shape);
   const int64_t n_tiles = (shape->k + 255) / 256;
   const int64_t tiles = (m + 127) / 128 * n_tiles;

@@ -72,7 +72,7 @@ def test_splitk_needs_two_kblocks():
 
 
 def test_dispatch_policy_on_baseline():
-    want = {"cfg4b_small_3x3": "splitk", "cfg4c_tail_k100": "generic",
+    want = {"cfg4b_small_3x3": "splitk", "cfg4c_tail_k100": "halo",
             "cfg5a_stress_3x3": "generic", "cfg5b_dilated_3x3": "generic",
             "cfg3b_pointwise": "generic"}
     table = m.load_workloads()
@@ -84,15 +84,24 @@ def test_narrow_generic_tiles_take_the_small_odd_k_layer():
     # GENERIC runs narrow N tiles where its tiles fill less than one wave
     # and bn is not a multiple of 64 (int8conv_rules.h, i8c_generic_bn); of
     # the 51 workloads only 4c (K = 100, bn 112 -> four 32-column tiles)
-    # qualifies, and there GENERIC beat SPLITK on B200 (13.4-13.8 against
-    # 15.1-15.2 us per launch).
+    # qualifies.  There GENERIC beat SPLITK on B200 (13.4-13.8 against
+    # 15.1-15.2 us per launch) and HALO, which stages each row tile's taps
+    # once instead of once per narrow tile, beat GENERIC (6.1 against 7.0 us
+    # per launch in graph replay), so such a layer runs HALO where HALO is
+    # eligible and GENERIC elsewhere.
     # smoke (K = 32, nine k-blocks) takes GENERIC by the k-block threshold
     # of split-K instead (test_splitk_needs_ten_kblocks).
     table = m.load_workloads()
-    picked = {name for name, s in table.items()
-              if s.select() == "generic" and s.eligible("splitk") and s.k % 64 != 0
-              and (s.n * s.out_h * s.out_w + 127) // 128 < 148}
-    assert picked == {"cfg4c_tail_k100", "smoke"}
+    small_odd = {name for name, s in table.items()
+                 if s.select() in ("generic", "halo") and s.eligible("splitk") and s.k % 64 != 0
+                 and (s.n * s.out_h * s.out_w + 127) // 128 < 148}
+    assert small_odd == {"cfg4c_tail_k100", "smoke"}
+    assert table["cfg4c_tail_k100"].select() == "halo"
+    assert table["smoke"].select() == "generic"
+    # Without HALO (a stride of 2) the same narrow-tile layer stays GENERIC.
+    s = table["cfg4c_tail_k100"]
+    strided = m.ConvShape(s.n, 2 * s.h, 2 * s.w, s.c, s.k, s.r, s.s, s.pad_h, s.pad_w, 2, 2)
+    assert not strided.eligible("halo") and strided.select() == "generic"
 
 
 def test_splitk_needs_ten_kblocks():
@@ -236,7 +245,7 @@ def test_generic_eligible_is_shape_valid():
             dilation_h=int(rng.randint(1, 20)), dilation_w=int(rng.randint(1, 20)))
         assert s.eligible("generic") == s.valid, s
         if s.valid:
-            assert s.select() in ("generic", "splitk"), s
+            assert s.select() in ("generic", "splitk", "halo"), s
             if not im2col_encodable(s):
                 seen_beyond += 1
                 assert s.select() == "generic"
