@@ -1248,11 +1248,19 @@ static bool plan_geometry(const int8conv_shape &s, int mode, bool pair, int out_
   g.store_maps = 0;
   if (mode == kModeStrip && out_kind == kOutInt32 && s.k % 4 == 0 &&
       (g.bn % 32 == 0 || g.n_tiles == 1)) {
+    // Every padded row ends in a run of Wp - Q dropped positions.  With at
+    // least 32 valid positions between runs a block meets one run at most;
+    // otherwise (short rows) count over the Wp block starts, which repeat.
+    const int run = g.Wp - g.Q;
     int most = 0;
-    for (int t = 0; t < g.Wp; ++t) {  // block starts 32 t mod Wp repeat within Wp blocks
-      int dropped = 0;
-      for (int r = 0; r < 32; ++r) dropped += (32 * t + r) % g.Wp >= g.Q ? 1 : 0;
-      if (dropped > most) most = dropped;
+    if (g.Q >= 32) {
+      most = run < 32 ? run : 32;
+    } else {
+      for (int t = 0; t < g.Wp; ++t) {
+        int dropped = 0;
+        for (int r = 0; r < 32; ++r) dropped += (32 * t + r) % g.Wp >= g.Q ? 1 : 0;
+        if (dropped > most) most = dropped;
+      }
     }
     if (most + 1 <= kMaxStoreMaps) {
       g.store_maps = most + 1;
