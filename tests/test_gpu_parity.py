@@ -394,3 +394,28 @@ def test_no_writes_outside_the_output(cuda, pairing, name):
         assert np.all(host[:g] == 0x5A5A5A5A), f"{fam} wrote before the output"
         assert np.all(host[g + shape.output_elements:] == 0x5A5A5A5A), f"{fam} wrote past it"
         assert np.array_equal(host[g:g + shape.output_elements], want), fam
+
+
+# STRIP's int32 epilogue stores each block of 32 padded positions as its valid
+# rows, compacted, through the output map whose box has that many rows; the
+# planner counts the dropped positions per block in closed form when a row
+# has at least 32 outputs and by scanning the block starts otherwise, and
+# falls back to 16-byte stores when more than eight maps would be needed or
+# a block (the grid's tail) holds fewer valid rows than any map.
+STRIP_STORE_SHAPES = {
+    "closed_form_q40": m.ConvShape(3, 9, 40, 32, 64, 3, 3, 1, 1),      # Q = 40, 2 dropped per row
+    "scan_q20": m.ConvShape(5, 7, 20, 32, 96, 3, 3, 1, 1),            # Q = 20, Wp = 22
+    "fallback_q12_s5": m.ConvShape(4, 6, 12, 32, 64, 5, 5, 2, 2),     # Wp = 16: 8 dropped of 32
+    "tail_q33_k36": m.ConvShape(1, 5, 33, 48, 36, 3, 3, 1, 1),        # Mp not a multiple of 32
+    "wide_q70_s7": m.ConvShape(2, 4, 70, 16, 128, 1, 7, 0, 3),        # 6 dropped per row
+}
+
+
+@pytest.mark.parametrize("name", sorted(STRIP_STORE_SHAPES))
+def test_strip_compacted_stores(cuda, pairing, name):
+    shape = STRIP_STORE_SHAPES[name]
+    assert shape.eligible("strip"), name
+    x, w, b = m.make_inputs(shape)
+    want = pyoracle.conv(shape, x, w, b)
+    got = _run(cuda, "strip", shape, x, w, b)
+    assert np.array_equal(got, want), f"strip differs from the oracle on {name}"
